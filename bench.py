@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 quantization hot path on B200.
+
+One step = the row-sharded quantization of BASELINE config 5: an activation
+X (65536 x 14336 bf16, N(0,1) with 0.1% x50 outliers) is split by row blocks
+across the ranks (API view: m = 14336, n = 65536 / N columns per rank), and
+each rank runs
+    global-amax pre-pass (nvfp4_amax_bf16)
+    -> NCCL max-allreduce of the scalar (N > 1 only)
+    -> RHT GEMM + NVFP4 cast with stochastic rounding
+       (nvfp4_rht_gemm_ntt_w_sfc_sharded, global RNG coordinates).
+`value` is GB/s in the reference's byte convention for the cast
+(2.5625 B per element: 2 read + 0.5 FP4 + 0.0625 SFC, rht_gemm/test_compare.cu:256)
+over all ranks' elements divided by the max-over-ranks step time; the amax
+pass is inside the step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own CPU implementation of the path
+(NaiveReference from rht_gemm/test_correctness.cu, compiled in place into
+oracle/_ref/libref_cpu.so) on the host cores, on a bounded sample of the same
+workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 65536, 14336          # activation X (tokens x features)
+BYTES_PER_ELEM = 2 + 0.5 + 1.0 / 16
+RHT_FIXED_BYTES = 512 + 4          # B matrix + amax
+SEED = 20260101
+NOMINAL_HBM_GBS = 8000.0
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.proc = None
+        self.idx = ",".join(str(i) for i in gpu_indices)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.idx, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_shard(torch, rank, n_cols):
+    """This rank's shard of X: rows [rank*n_cols, (rank+1)*n_cols), which in the
+    API's column-major view is an m x n_cols matrix (contiguous)."""
+    g = torch.Generator(device="cuda").manual_seed(SEED + rank)
+    x = torch.randn(n_cols * COLS, device="cuda", dtype=torch.float32, generator=g)
+    mask = torch.rand(n_cols * COLS, device="cuda", generator=g) < 0.001
+    x[mask] *= 50.0
+    out = x.to(torch.bfloat16)
+    del x, mask
+    return out
+
+
+class CpuReference:
+    """The reference's own CPU implementation of the path (NaiveReference,
+    rht_gemm/test_correctness.cu:110-198, compiled in place into
+    oracle/_ref/libref_cpu.so; kind "reference"), or the oracle port when that
+    library is absent (kind "port"), on a bounded column slice of the
+    workload: API m = 14336 rows x `ncols` columns, sized so one call takes
+    about `target_s` seconds."""
+
+    def __init__(self, target_s: float, threads: int | None = None):
+        from oracle import oracle, ref
+        self.oracle, self.ref = oracle, ref
+        self.threads = threads or os.cpu_count() or 1
+        self.kind = "reference" if ref.cpu_available() else "port"
+        i = np.arange(16)
+        par = np.array([[bin(a & b).count("1") & 1 for b in i] for a in i])
+        self.B = oracle.f32_to_bf16(np.where(par == 0, 0.25, -0.25).astype(np.float32))
+        self.m = COLS
+        self.rng = np.random.default_rng(SEED)
+        ncols = 64 * self.threads
+        dt = self._size(ncols)
+        while dt < target_s / 8 and ncols < ROWS:
+            ncols = min(ROWS, ncols * 4)
+            dt = self._size(ncols)
+        ncols = int(min(ROWS, max(64, ncols * target_s / max(dt, 1e-3))) // 64 * 64)
+        self._size(ncols)
+
+    def _size(self, ncols):
+        self.ncols = ncols
+        self.A = self.oracle.f32_to_bf16(self.rng.standard_normal(self.m * ncols)
+                                         .astype(np.float32))
+        self.C = np.zeros((self.m, ncols // 2), np.uint8)
+        self.S = np.zeros((self.m, ncols // 16), np.uint8)
+        return self.step()
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            self.ref.cpu().ref_naive_rht(self.m, self.ncols, self.A.ctypes.data,
+                                         self.B.ctypes.data, self.C.ctypes.data,
+                                         self.S.ctypes.data, 4.0, 0, 64, self.threads)
+        else:
+            self.oracle.rht_gemm_ntt_w_sfc(self.m, self.ncols, self.A, self.B, 4.0, (SEED, 0),
+                                           2048, True, False)
+        return time.perf_counter() - t0
+
+    @property
+    def elems(self):
+        return self.m * self.ncols
+
+    def describe(self, dt):
+        if self.kind == "reference":
+            return (f"NaiveReference::compute (rht_gemm/test_correctness.cu:110-198; "
+                    f"round-to-nearest, the reference has no CPU stochastic-rounding RHT) on "
+                    f"API m={self.m} x n={self.ncols} columns of the workload, "
+                    f"{self.threads} threads, {dt:.2f} s per step")
+        return f"oracle port (SR) on m={self.m} x n={self.ncols}, 1 thread, {dt:.2f} s"
+
+    def baseline(self, steps=1):
+        ts = sorted(self.step() for _ in range(steps))
+        dt = ts[len(ts) // 2]
+        return {"value": self.elems * BYTES_PER_ELEM / dt / 1e9, "unit": "GB/s",
+                "elem_per_s": self.elems / dt,
+                "cores": self.threads if self.kind == "reference" else 1,
+                "kind": self.kind, "sample": self.describe(dt)}
+
+
+def bench_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    cpu = CpuReference(target_s=float(os.environ.get("NVFP4_CPU_STEP_S", "1.5")))
+    for _ in range(args.warmup):
+        cpu.step()
+    base = cpu.baseline(args.steps)
+    line = {
+        "metric": "RHT+NVFP4 quant HBM GB/s (frac of 8 TB/s) and elem/s at 1/2/4/8 B200",
+        "impl": "reference",
+        "value": round(base["value"], 3),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": None,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "elem_per_s": base["elem_per_s"],
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(base["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(n):
+    return {"workload": "BASELINE cfg5: X 65536x14336 bf16 N(0,1)+0.1% x50 outliers, "
+                        "row-sharded (API m=14336, n=65536/N per rank), amax pre-pass + "
+                        "NCCL max-allreduce + RHT GEMM + NVFP4 cast, stochastic rounding",
+            "m": COLS, "n_total": ROWS, "n_per_rank": ROWS // n, "k_tile_size": 2048,
+            "stochastic_rounding": True, "parallelism": f"row-shard x{n}",
+            "l2": "inputs larger than L2 (per-rank shard >= 235 MB > 126 MB)"}
+
+
+def bench_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    if ws != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    import fp4_sm120a_b200 as nv
+    nv.load()
+    m = COLS
+    n_total = ROWS
+    n = n_total // ws
+    A = make_shard(torch, rank, n)
+    B = nv.hadamard16(torch.where(torch.arange(16) % 3 == 0, -1.0, 1.0), device="cuda")
+    C = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
+    S = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
+    amax = torch.empty(1, dtype=torch.float32, device="cuda")
+    rng_state = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        nv.amax_bf16(A, m * n, amax, stream)
+        if ws > 1:
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+        if ev is not None:
+            ev[0].record(stream)
+        nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, rank * n, n_total, 0,
+                                      stream, 2048, stochastic_rounding=True)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if nv.device_error() != 0:
+        raise SystemExit("kernel reported a device timeout")
+
+    gpu_list = [local] if ws == 1 else list(range(ws))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(gpu_list) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    if sampler:
+        sampler.__exit__()
+    ms_total = t0.elapsed_time(t1)
+    rht_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    tt = torch.tensor([ms_total, rht_ms], dtype=torch.float64, device="cuda")
+    if ws > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_total, rht_ms = tt.tolist()
+    ms_step = ms_total / args.steps
+    elems_total = m * n_total
+    value = elems_total * BYTES_PER_ELEM / (ms_step * 1e-3) / 1e9
+
+    # ---------------- end to end through the public API, host buffers -------
+    e2e_steps = max(1, min(args.steps, 3))
+    hA = torch.empty(A.numel(), dtype=torch.bfloat16, pin_memory=True)
+    hA.copy_(A)
+    hC = torch.empty(C.shape, dtype=torch.uint8, pin_memory=True)
+    hS = torch.empty(S.shape, dtype=torch.uint8, pin_memory=True)
+    dA = torch.empty_like(A)
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        nv.amax_bf16(dA, m * n, amax, stream)
+        if ws > 1:
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+        nv.rht_gemm_ntt_w_sfc_sharded(m, n, dA, B, C, S, amax, rng_state, rank * n, n_total, 0,
+                                      stream, 2048, stochastic_rounding=True)
+        hC.copy_(C, non_blocking=True)
+        hS.copy_(S, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device="cuda")
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = te.item()
+    # output check of the e2e path against the device-resident path
+    same = bool(torch.equal(hC[:4].cuda(), C[:4]))
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        rht_bytes = m * n * BYTES_PER_ELEM + RHT_FIXED_BYTES
+        achieved = rht_bytes / (rht_ms * 1e-3) / 1e9
+        traffic = None
+        tp = ROOT / "profiles" / "rht_nvfp4_traffic.json"
+        if tp.exists():
+            t = json.loads(tp.read_text())
+            traffic = round(t["dram_bytes_per_element"] * m * n)
+        clocks = sampler.summary() if sampler else {}
+        line = {
+            "metric": "RHT+NVFP4 quant HBM GB/s (frac of 8 TB/s) and elem/s at 1/2/4/8 B200",
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 with 0.1% x50 outliers; BASELINE cfg5 shape)",
+            "config": workload_config(ws),
+            "elem_per_s": elems_total / (ms_step * 1e-3),
+            "frac_of_8TBs": round(value / NOMINAL_HBM_GBS, 4),
+            "step_hbm_gbs": round(elems_total * (BYTES_PER_ELEM + 2.0) / (ms_step * 1e-3) / 1e9,
+                                  2),
+            "roofline": {"bound": "hbm", "kernel": "rht_nvfp4_kernel<SR=1,FM=0>",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_launch": rht_bytes,
+                         "avg_launch_ms": round(rht_ms, 5)},
+            "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
+                       "reasons": clocks.get("reasons", []), "samples": clocks.get("samples")},
+            "e2e": {"value": round(elems_total * BYTES_PER_ELEM / (e2e_ms * 1e-3) / 1e9, 3),
+                    "unit": "GB/s", "h2d_bytes_per_step": A.numel() * 2,
+                    "d2h_bytes_per_step": C.numel() + S.numel(), "ms_per_step": round(e2e_ms, 3),
+                    "matches_device_path": same},
+            "gpu_launches": 2 * args.steps,
+        }
+        if ws == 1 and not args.no_cpu_baseline:
+            base = CpuReference(float(os.environ.get("NVFP4_CPU_STEP_S", "3"))).baseline(3)
+            line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind",
+                                                         "sample")}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return bench_reference(args)
+    return bench_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

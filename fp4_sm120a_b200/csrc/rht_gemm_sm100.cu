@@ -1,0 +1,641 @@
+// RHT GEMM fused with the NVFP4 cast, written for B200 (sm_100a).
+//
+// Computes, for an m x n column-major bf16 matrix A and a 16 x 16 bf16 matrix B,
+// C[:, 16g:16g+16] = A[:, 16g:16g+16] * B for every 16-column group g, then
+// quantizes each (row, group) 16-vector to NVFP4: one E4M3 scale from the
+// vector's amax and the global amax, sixteen E2M1 codes by stochastic rounding
+// (Philox4x32-10 in Transformer Engine's coordinate mapping) or by
+// round-to-nearest.  Results are bit-identical to TE's SM100 kernel
+// (rht_gemm/te_ref/hadamard_transform_cast_fusion_core.inc:92-506).
+//
+// Design (persistent, warp-specialised, one CTA per SM):
+//   work unit   128 rows x 256 columns of A (one output tile)
+//   warp 0      TMA producer: 128 x 64 bf16 sub-tiles (two 64 x 64 boxes,
+//               128-byte swizzle) into an 8-stage shared-memory ring
+//   warp 1      tcgen05.mma issuer: per sub-tile four M128 N16 K16 bf16 MMAs
+//               (one per 16-column group) into a 4-stage TMEM ring of
+//               128-column fp32 accumulators; owns the TMEM allocation
+//   warps 2-17  epilogue: tcgen05.ld of a 32-column slice of its 32 TMEM lanes,
+//               bf16 round trip, amax, E4M3 scale, reciprocal, Philox, cvt.rs /
+//               cvt.rn; FP4 bytes staged in a swizzled 128 x 128 B tile that one
+//               TMA store writes out; scale bytes staged and copied out in
+//               16-byte rows.
+// Every wait is bounded (1 s); a kernel that gives up records an error word
+// and unwinds (drains its TMA loads and MMAs, frees TMEM) instead of hanging.
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "launch_common.h"
+#include "nvfp4_b200.h"
+#include "nvfp4_device.cuh"
+
+namespace nvfp4 {
+
+// Error word of this device (see nvfp4_device_error).
+__device__ uint32_t g_device_error_word;
+
+namespace rht {
+
+constexpr int kBM = 128;          // rows per tile = TMEM lanes
+constexpr int kSubN = 64;         // columns per TMA sub-tile
+constexpr int kUnitN = 256;       // columns per work unit / output tile
+constexpr int kAccN = 128;        // fp32 columns per TMEM accumulator stage
+constexpr int kStages = 8;        // shared-memory ring depth
+constexpr int kAccStages = 4;     // 4 x 128 = all 512 TMEM columns
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr uint32_t kStageBytes = kBM * kSubN * 2;        // 16 KiB
+constexpr uint32_t kHalfBytes = kStageBytes / 2;         // one 64 x 64 box
+constexpr uint32_t kCTileBytes = kBM * kUnitN / 2;       // 16 KiB
+constexpr uint32_t kSfcTileBytes = kBM * kUnitN / 16;    // 2 KiB
+constexpr uint64_t kWaitLimitNs = 1000000000ull;         // 1 s per wait
+
+constexpr uint32_t kOffA = 0;
+constexpr uint32_t kOffC = kOffA + kStages * kStageBytes;
+constexpr uint32_t kOffSfc = kOffC + 2 * kCTileBytes;
+constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
+constexpr uint32_t kOffBar = kOffB + 512;
+constexpr uint32_t kNumBars = 2 * kStages + 2 * kAccStages + 1;
+constexpr uint32_t kOffMisc = kOffBar + 8 * kNumBars;
+constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
+
+// tcgen05 instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B,
+// both MN-major, N = 16, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+                            ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+struct Params {
+  int m, n;
+  int tiles_m;        // m / 128
+  int units;          // tiles_m * ceil(n / 256)
+  int n_offset;       // column offset of this shard in the full problem
+  uint32_t ktm;       // TE's K_TILE_MAX = min(n_total, k_tile_size) / 64
+  int sfc_vec;        // bytes per SFC store: 16, 4 or 1
+  const uint16_t* B;
+  uint8_t* sfc;
+  const float* amax;
+  const size_t* rng;
+};
+
+struct Unit {
+  int tm, m0, n0, nsub, nacc;
+};
+__device__ __forceinline__ Unit decode_unit(const Params& p, int u) {
+  Unit t;
+  t.tm = u % p.tiles_m;
+  t.m0 = t.tm * kBM;
+  t.n0 = (u / p.tiles_m) * kUnitN;
+  const int rem = (p.n - t.n0) / kSubN;
+  t.nsub = rem < 4 ? rem : 4;
+  t.nacc = (t.nsub + 1) / 2;
+  return t;
+}
+
+// Quantize one 16-vector in place: TE epilogue math (core.inc:439-492).
+template <bool SR, bool FM>
+__device__ __forceinline__ uint32_t quant16(float* x, float enc_mult, float dec, uint4 rb,
+                                            uint32_t& w0, uint32_t& w1) {
+  if constexpr (!FM) {
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) bf16_round_pair(x[k], x[k + 1]);
+  }
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) am = fmax_nan(am, fabsf(x[k]));
+  const uint32_t code = e4m3_encode(am * enc_mult);
+  const float qs = e4m3_decode(code) * dec;
+  float acc = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
+  acc = fmin_nan(acc, 3.402823466e38f);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = x[k] * acc;
+  if constexpr (SR) {
+    w0 = (uint32_t)sr_e2m1x4(x[0], x[1], x[2], x[3], rb.x) |
+         ((uint32_t)sr_e2m1x4(x[4], x[5], x[6], x[7], rb.y) << 16);
+    w1 = (uint32_t)sr_e2m1x4(x[8], x[9], x[10], x[11], rb.z) |
+         ((uint32_t)sr_e2m1x4(x[12], x[13], x[14], x[15], rb.w) << 16);
+  } else {
+    w0 = rn_e2m1x2(x[0], x[1]) | (rn_e2m1x2(x[2], x[3]) << 8) | (rn_e2m1x2(x[4], x[5]) << 16) |
+         (rn_e2m1x2(x[6], x[7]) << 24);
+    w1 = rn_e2m1x2(x[8], x[9]) | (rn_e2m1x2(x[10], x[11]) << 8) |
+         (rn_e2m1x2(x[12], x[13]) << 16) | (rn_e2m1x2(x[14], x[15]) << 24);
+  }
+  return code;
+}
+
+// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
+                                          volatile uint32_t* abort_flag, uint32_t err) {
+  uint32_t ok = 0;
+  if ((threadIdx.x & 31) == 0)
+    ok = mbar_wait_bounded(bar, parity, abort_flag, kWaitLimitNs, err, &g_device_error_word);
+  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
+}
+
+template <bool SR, bool FM>
+__global__ void __launch_bounds__(kThreads, 1)
+    rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmC, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const uint32_t bar0 = sbase + kOffBar;
+  auto full_bar = [&](uint32_t s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](uint32_t s) { return bar0 + 8 * (kStages + s); };
+  auto accf_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + a); };
+  auto acce_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + kAccStages + a); };
+  const uint32_t drain_bar = bar0 + 8 * (2 * kStages + 2 * kAccStages);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (uint32_t a = 0; a < kAccStages; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    // B into shared memory in the canonical no-swizzle MN-major layout:
+    // B(n = c, k) at (c % 8) * 2 + (k % 8) * 16 + (c / 8) * 128 + (k / 8) * 256.
+    uint16_t* sb = reinterpret_cast<uint16_t*>(smem + kOffB);
+    for (int idx = lane; idx < 256; idx += 32) {
+      const int k = idx >> 4, c = idx & 15;
+      const uint32_t off = (c & 7) * 2 + (k & 7) * 16 + (c >> 3) * 128 + (k >> 3) * 256;
+      sb[off >> 1] = p.B[idx];
+    }
+    fence_proxy_async_smem();
+    tmem_alloc(smem_addr(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit t = decode_unit(p, u);
+        for (int s = 0; s < t.nsub; ++s) {
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutProducer, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
+          const uint32_t dst = sbase + kOffA + stage * kStageBytes;
+          const int y = t.n0 + s * kSubN;
+          tma_load_2d(dst, &tmA, full_bar(stage), t.m0, y);
+          tma_load_2d(dst + kHalfBytes, &tmA, full_bar(stage), t.m0 + 64, y);
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // Let the loads already in flight land before the CTA exits.
+        uint32_t st = stage, ph = phase;
+        const uint32_t n_pending = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+        volatile uint32_t never = 0u;
+        for (uint32_t i = 0; i < n_pending; ++i) {
+          if (st == 0) { st = kStages - 1; ph ^= 1u; } else { --st; }
+          mbar_wait_bounded(full_bar(st), ph, &never, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      const uint64_t bdesc = umma_smem_desc(sbase + kOffB, 256, 128, 0);
+      uint32_t stage = 0, phase = 0, acc = 0, accph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit t = decode_unit(p, u);
+        for (int a = 0; a < t.nacc && ok; ++a) {
+          if (!mbar_wait_bounded(acce_bar(acc), accph ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutMma, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nh = (t.nsub - 2 * a) < 2 ? (t.nsub - 2 * a) : 2;
+          for (int h = 0; h < nh; ++h) {
+            if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, kWaitLimitNs,
+                                   kErrTimeoutMma, &g_device_error_word)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = sbase + kOffA + stage * kStageBytes;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              // A: 128 (m) x 16 (k) MN-major, 128-byte swizzle; the two 64-row
+              // halves are 8 KiB apart (LBO), 8-column groups 1 KiB apart (SBO).
+              const uint64_t adesc = umma_smem_desc(a_base + g * 2048, kHalfBytes, 1024, 2);
+              tc_mma_f16_overwrite(tmem_base + acc * kAccN + h * kSubN + g * 16, adesc, bdesc,
+                                   kIdesc);
+            }
+            tc_commit(empty_bar(stage));
+            if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          tc_commit(accf_bar(acc));
+          if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
+        }
+      }
+      // All issued MMAs complete before TMEM is released.
+      tc_commit(drain_bar);
+      volatile uint32_t never = 0u;
+      mbar_wait_bounded(drain_bar, 0, &never, kWaitLimitNs, kErrTimeoutDrain,
+                        &g_device_error_word);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ----------------------------------
+    const int ew = warp - 2;
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int slice = ew >> 2;        // 32-column slice of each accumulator stage
+    const int r = q * 32 + lane;      // row within the 128-row tile
+    const bool leader = (ew == 0 && lane == 0);
+
+    const float enc = global_encode_scale(*p.amax);
+    const float dec = __fdiv_rn(1.0f, enc);
+    const float enc_mult = enc * (1.0f / 6.0f);
+    uint64_t seed = 0, offset = 0;
+    if (SR && p.rng != nullptr) {
+      seed = p.rng[0];
+      offset = p.rng[1];
+    }
+    const int sfc_row_bytes = p.n / 16;
+
+    uint32_t acc = 0, accph = 0, ucount = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++ucount) {
+      const Unit t = decode_unit(p, u);
+      const uint32_t buf = ucount & 1u;
+      uint8_t* cst = smem + kOffC + buf * kCTileBytes;
+      uint8_t* sst = smem + kOffSfc + buf * kSfcTileBytes;
+      for (int a = 0; a < t.nacc && ok; ++a) {
+        if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int blk = 2 * a + (slice >> 1);  // 64-column block within the unit
+        const bool valid = blk < t.nsub;
+        float v[32];
+        if (valid) {
+          tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
+          tc_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar(acc));
+        if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
+        if (!valid) continue;
+
+        uint4 rb0 = make_uint4(0, 0, 0, 0), rb1 = rb0;
+        if constexpr (SR) {
+          // TE: seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
+          // linear_tile = tile_m + tiles_m * (k_block / K_TILE_MAX), one
+          // generate4() per 16 columns of the 64-column k-tile.
+          const uint32_t kb = (uint32_t)((p.n_offset + t.n0) / kSubN) + (uint32_t)blk;
+          const uint32_t chunk = kb / p.ktm;
+          const uint32_t L = (uint32_t)t.tm + (uint32_t)p.tiles_m * chunk;
+          const uint32_t seq = (uint32_t)r + (kb - chunk * p.ktm) * 256u + L * p.ktm * 256u;
+          Philox ph;
+          ph.init(seed, (uint64_t)seq, offset, (uint32_t)(slice & 1) * 2u);
+          rb0 = ph.generate4();
+          rb1 = ph.generate4();
+        }
+        uint32_t w0, w1, w2, w3;
+        const uint32_t s0 = quant16<SR, FM>(v, enc_mult, dec, rb0, w0, w1);
+        const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, dec, rb1, w2, w3);
+        // swizzled (128-byte pattern) FP4 tile row r, 16-byte chunk a*4+slice
+        const uint32_t chunk16 = (uint32_t)(a * 4 + slice) ^ (uint32_t)(r & 7);
+        *reinterpret_cast<uint4*>(cst + r * 128 + chunk16 * 16) = make_uint4(w0, w1, w2, w3);
+        *reinterpret_cast<uint16_t*>(sst + r * 16 + a * 8 + slice * 2) =
+            (uint16_t)(s0 | (s1 << 8));
+      }
+      // One barrier per unit among the epilogue warps.  Before it, the leader
+      // waits until the previous TMA store has read its staging buffer, which
+      // the next unit will overwrite.
+      fence_proxy_async_smem();
+      if (leader) bulk_wait_read_all();
+      __syncwarp();
+      named_bar_sync(1, kEpiThreads);
+      if (!ok || *abort_flag) {
+        ok = false;
+        continue;
+      }
+      if (leader) {
+        tma_store_2d(&tmC, smem_addr(cst), t.n0 / 2, t.m0);
+        bulk_commit();
+      }
+      if (ew < 4) {
+        const int row = ew * 32 + lane;
+        uint8_t* dst = p.sfc + (size_t)(t.m0 + row) * sfc_row_bytes + t.n0 / 16;
+        const uint8_t* src = sst + row * 16;
+        const int nbytes = t.nsub * 4;
+        if (p.sfc_vec == 16 && nbytes == 16) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else if (p.sfc_vec >= 4) {
+          for (int b = 0; b < nbytes; b += 4)
+            *reinterpret_cast<uint32_t*>(dst + b) = *reinterpret_cast<const uint32_t*>(src + b);
+        } else {
+          for (int b = 0; b < nbytes; ++b) dst[b] = src[b];
+        }
+      }
+    }
+    if (leader) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t ptr;
+  uint64_t d0, d1;
+  int kind;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<uint64_t>()(k.d0 * 1315423911u + k.d1) << 1) ^
+           (size_t)k.kind;
+  }
+};
+
+// Encoded tensor maps are cached by (address, shape); encoding costs a few
+// microseconds of host time per call otherwise.
+int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, kind};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return NVFP4_OK;
+    }
+  }
+  auto fn = encode_fn();
+  if (!fn) return cuda_status(cudaErrorNotSupported);
+  CUtensorMap map;
+  CUresult res;
+  const cuuint32_t estride[2] = {1, 1};
+  if (kind == 0) {
+    // A: bf16, dims {m, n}, box 64 x 64, 128-byte swizzle
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {d0 * 2};
+    const cuuint32_t box[2] = {64, 64};
+    res = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // C: bytes, dims {n/2, m}, box 128 x 128, 128-byte swizzle
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {d0};
+    const cuuint32_t box[2] = {128, 128};
+    res = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ptr, dims, strides, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (res != CUDA_SUCCESS) return NVFP4_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 256) cache.clear();
+  cache.emplace(key, map);
+  *out = map;
+  return NVFP4_OK;
+}
+
+template <bool SR, bool FM>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p, int grid,
+                  cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kSmemBytes))
+      return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  rht_nvfp4_kernel<SR, FM><<<grid, kThreads, kSmemBytes, stream>>>(ta, tc, p);
+  return cuda_status(cudaGetLastError());
+}
+
+int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
+               const float* global_amax, const size_t* rng_state, uint32_t sm_count,
+               cudaStream_t stream, int k_tile_size, int sr, int fm, int n_offset, int n_total) {
+  if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
+  if (m == 0 || n == 0) return NVFP4_OK;
+  if (m % kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
+  if (n_total <= 0) n_total = n;
+  if (n_offset < 0 || n_offset + n > n_total) return NVFP4_ERR_INVALID_SHAPE;
+  const int kt = n_total < k_tile_size ? n_total : k_tile_size;
+  const uint32_t ktm = (uint32_t)(kt / 64);
+  if (n_offset % (int)(ktm * 64) != 0) return NVFP4_ERR_INVALID_SHAPE;
+  if (!A || !B || !C || !SFC || !global_amax) return NVFP4_ERR_INVALID_ARGUMENT;
+  if ((uintptr_t)A % 16 || (uintptr_t)C % 16 || (uintptr_t)B % 2) return NVFP4_ERR_MISALIGNED;
+  int sms = 0;
+  if (int e = device_sm_count(&sms)) return e;
+
+  CUtensorMap ta, tc;
+  if (int e = get_tensor_map(0, const_cast<void*>(A), (uint64_t)m, (uint64_t)n, &ta)) return e;
+  if (int e = get_tensor_map(1, C, (uint64_t)(n / 2), (uint64_t)m, &tc)) return e;
+
+  Params p;
+  p.m = m;
+  p.n = n;
+  p.tiles_m = m / kBM;
+  p.units = p.tiles_m * ((n + kUnitN - 1) / kUnitN);
+  p.n_offset = n_offset;
+  p.ktm = ktm;
+  const uintptr_t sfc_addr = reinterpret_cast<uintptr_t>(SFC);
+  p.sfc_vec = ((n / 16) % 16 == 0 && sfc_addr % 16 == 0) ? 16 : (sfc_addr % 4 == 0 ? 4 : 1);
+  p.B = reinterpret_cast<const uint16_t*>(B);
+  p.sfc = reinterpret_cast<uint8_t*>(SFC);
+  p.amax = global_amax;
+  p.rng = rng_state;
+
+  int grid = sms;
+  if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
+  if (p.units < grid) grid = p.units;
+
+  if (sr && fm) return launch_kernel<true, true>(ta, tc, p, grid, stream);
+  if (sr) return launch_kernel<true, false>(ta, tc, p, grid, stream);
+  if (fm) return launch_kernel<false, true>(ta, tc, p, grid, stream);
+  return launch_kernel<false, false>(ta, tc, p, grid, stream);
+}
+
+}  // namespace rht
+
+// ---------------------------------------------------------------------------
+// Shared host helpers
+// ---------------------------------------------------------------------------
+namespace {
+thread_local int t_last_cuda_error = 0;
+}
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return NVFP4_OK;
+  t_last_cuda_error = (int)e;
+  return NVFP4_ERR_CUDA;
+}
+
+int device_sm_count(int* sms) {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
+  if (dev < 64 && cache[dev] > 0) {
+    *sms = cache[dev];
+    return NVFP4_OK;
+  }
+  int major = 0, minor = 0, count = 0;
+  if (cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev))
+    return cuda_status(e);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return NVFP4_ERR_UNSUPPORTED_DEVICE;
+  if (cudaError_t e = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev))
+    return cuda_status(e);
+  if (dev < 64) cache[dev] = count;
+  *sms = count;
+  return NVFP4_OK;
+}
+
+}  // namespace nvfp4
+
+using nvfp4::rht::rht_launch;
+
+extern "C" {
+
+NVFP4_API const char* nvfp4_status_string(int status) {
+  switch (status) {
+    case NVFP4_OK: return "ok";
+    case NVFP4_ERR_INVALID_SHAPE: return "invalid shape (m % 128, n % 64, cols % 16 or k_tile_size)";
+    case NVFP4_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or bad flags)";
+    case NVFP4_ERR_MISALIGNED: return "misaligned pointer";
+    case NVFP4_ERR_CUDA: return "CUDA runtime error";
+    case NVFP4_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs compute capability 10.0)";
+    case NVFP4_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out";
+    default: return "unknown status";
+  }
+}
+
+NVFP4_API int nvfp4_last_cuda_error(void) { return nvfp4::t_last_cuda_error; }
+
+NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc(int m, int n, const void* A, const void* B, void* C,
+                                       void* SFC, const float* global_amax,
+                                       const size_t* rng_state, uint32_t sm_count,
+                                       nvfp4_stream_t stream, int k_tile_size,
+                                       int stochastic_rounding, int use_fast_math) {
+  return rht_launch(m, n, A, B, C, SFC, global_amax, rng_state, sm_count, (cudaStream_t)stream,
+                    k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n);
+}
+
+NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded(int m, int n, const void* A, const void* B,
+                                               void* C, void* SFC, const float* global_amax,
+                                               const size_t* rng_state, uint32_t sm_count,
+                                               nvfp4_stream_t stream, int k_tile_size,
+                                               int stochastic_rounding, int use_fast_math,
+                                               int n_offset, int n_total) {
+  return rht_launch(m, n, A, B, C, SFC, global_amax, rng_state, sm_count, (cudaStream_t)stream,
+                    k_tile_size, stochastic_rounding != 0, use_fast_math != 0, n_offset, n_total);
+}
+
+NVFP4_API int nvfp4_run_rht(int m, int n, const void* A, const void* B, void* C, void* SFC,
+                            const float* global_amax, const size_t* rng_state, uint32_t sm_count,
+                            nvfp4_stream_t stream) {
+  return nvfp4_rht_gemm_ntt_w_sfc(m, n, A, B, C, SFC, global_amax, rng_state, sm_count, stream,
+                                  2048, 0, 0);
+}
+NVFP4_API int nvfp4_run_rht_fast(int m, int n, const void* A, const void* B, void* C, void* SFC,
+                                 const float* global_amax, const size_t* rng_state,
+                                 uint32_t sm_count, nvfp4_stream_t stream) {
+  return nvfp4_rht_gemm_ntt_w_sfc(m, n, A, B, C, SFC, global_amax, rng_state, sm_count, stream,
+                                  2048, 0, 1);
+}
+NVFP4_API int nvfp4_run_rht_sr(int m, int n, const void* A, const void* B, void* C, void* SFC,
+                               const float* global_amax, const size_t* rng_state,
+                               uint32_t sm_count, nvfp4_stream_t stream) {
+  return nvfp4_rht_gemm_ntt_w_sfc(m, n, A, B, C, SFC, global_amax, rng_state, sm_count, stream,
+                                  2048, 1, 0);
+}
+
+NVFP4_API int nvfp4_rht_gemm_ttt(int m, int n, const void* A, const void* B, void* C, void* SFC,
+                                 const float* global_amax, const size_t* rng_state,
+                                 uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
+                                 int stochastic_rounding, int use_fast_math) {
+  return nvfp4_rht_gemm_ntt_w_sfc(n, m, A, B, C, SFC, global_amax, rng_state, sm_count, stream,
+                                  k_tile_size, stochastic_rounding, use_fast_math);
+}
+
+NVFP4_API int nvfp4_device_error(uint32_t* code, int clear) {
+  if (!code) return NVFP4_ERR_INVALID_ARGUMENT;
+  if (cudaError_t e = cudaDeviceSynchronize()) return nvfp4::cuda_status(e);
+  if (cudaError_t e = cudaMemcpyFromSymbol(code, nvfp4::g_device_error_word, sizeof(uint32_t)))
+    return nvfp4::cuda_status(e);
+  if (clear) {
+    const uint32_t zero = 0;
+    if (cudaError_t e = cudaMemcpyToSymbol(nvfp4::g_device_error_word, &zero, sizeof(uint32_t)))
+      return nvfp4::cuda_status(e);
+  }
+  return NVFP4_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,132 @@
+// nvfp4_sr.cuh -- drop-in device functions for FP4 (E2M1) stochastic rounding
+// on sm_100a, with the signatures, operand meaning and nibble order of the
+// reference's four functions:
+//
+//   mul_cvt_bf16_to_fp4_4x_with_stochastic_rounding
+//       replaces te_ref/stubs/common/util/ptx.cuh:563-598
+//       and stochastic_rounding/sr.sm120.cuh:112-142
+//   mul_cvt_fp32_to_fp4_4x_with_stochastic_rounding
+//       replaces ptx.cuh:660-689 and sr.sm120.cuh:153-177
+//   cvt_fp32_to_fp4_4x_with_stochastic_rounding
+//       replaces stochastic_rounding/compare.cuh:51-62 (native form)
+//       and sr.sm120.cuh:187-194
+//   mul_cvt_bf16_to_fp4_8x_stochastic_rounding<ScaleT>   (ScaleT = float or bf16)
+//       replaces ptx.cuh:839-918 and sr.sm120.cuh:205-240
+//
+// Semantics (all four): nibble k of the result is E2M1 of input element k
+// (times its scale), rounded stochastically by the native
+// cvt.rs.satfinite.e2m1x4.f32 with byte (3 - k mod 4) of the random word that
+// covers element k.  Element 0 sits in the low nibble.  4x forms scale even
+// elements by scale.x and odd elements by scale.y.  The 8x form takes one
+// scalar scale; with a bf16 scale the product is formed by fma(x, s, +0),
+// so a negative-zero product becomes +0 exactly as in the reference.
+//
+// Include from CUDA code compiled for sm_100a (or sm_103a).
+#pragma once
+
+#include <cstdint>
+#include <type_traits>
+#include <cuda_bf16.h>
+#if defined(__has_include)
+#if __has_include(<cuda_fp4.h>)
+#include <cuda_fp4.h>
+#define NVFP4_B200_HAVE_CUDA_FP4 1
+#endif
+#endif
+
+#ifndef NVFP4_B200_FP4X4_DEFINED
+#define NVFP4_B200_FP4X4_DEFINED
+#if defined(NVFP4_B200_HAVE_CUDA_FP4)
+using fp4e2m1x4 = __nv_fp4x4_e2m1;
+#else
+struct fp4e2m1x4 {
+  uint16_t __x;
+};
+#endif
+#endif
+
+namespace nvfp4_b200_detail {
+
+__device__ __forceinline__ float bf16_lane(uint64_t packed, int k) {
+  return __uint_as_float((uint32_t)((packed >> (16 * k)) & 0xFFFFu) << 16);
+}
+
+// Four fp32 values -> four E2M1 nibbles (x0 lowest), native stochastic rounding.
+__device__ __forceinline__ uint16_t rs4(float x0, float x1, float x2, float x3, uint32_t rbits) {
+  uint16_t r;
+  asm volatile("cvt.rs.satfinite.e2m1x4.f32 %0, {%1, %2, %3, %4}, %5;"
+               : "=h"(r)
+               : "f"(x3), "f"(x2), "f"(x1), "f"(x0), "r"(rbits));
+  return r;
+}
+
+__device__ __forceinline__ fp4e2m1x4 as_fp4x4(uint16_t bits) {
+  fp4e2m1x4 out;
+  static_assert(sizeof(fp4e2m1x4) == sizeof(uint16_t), "fp4e2m1x4 must be 16 bits");
+  __builtin_memcpy(&out, &bits, sizeof(bits));
+  return out;
+}
+
+// x * s with fma.rn.f32(x, s, +0): one rounding, and -0 products become +0.
+__device__ __forceinline__ float mul_plus_zero(float x, float s) {
+  float r;
+  asm("fma.rn.f32 %0, %1, %2, 0f00000000;" : "=f"(r) : "f"(x), "f"(s));
+  return r;
+}
+
+}  // namespace nvfp4_b200_detail
+
+// in_4x: four bf16 (element 0 in the low 16 bits).
+__device__ __forceinline__ fp4e2m1x4 mul_cvt_bf16_to_fp4_4x_with_stochastic_rounding(
+    const uint64_t in_4x, const float2 scale, const uint32_t rbits) {
+  using namespace nvfp4_b200_detail;
+  const float v0 = bf16_lane(in_4x, 0) * scale.x;
+  const float v1 = bf16_lane(in_4x, 1) * scale.y;
+  const float v2 = bf16_lane(in_4x, 2) * scale.x;
+  const float v3 = bf16_lane(in_4x, 3) * scale.y;
+  return as_fp4x4(rs4(v0, v1, v2, v3, rbits));
+}
+
+// Elements in order: in01.x, in01.y, in23.x, in23.y.
+__device__ __forceinline__ fp4e2m1x4 mul_cvt_fp32_to_fp4_4x_with_stochastic_rounding(
+    const float2 in01, const float2 in23, const float2 scale, const uint32_t rbits) {
+  using namespace nvfp4_b200_detail;
+  return as_fp4x4(rs4(in01.x * scale.x, in01.y * scale.y, in23.x * scale.x, in23.y * scale.y,
+                      rbits));
+}
+
+// No scale.  Elements in order: in01.x, in01.y, in23.x, in23.y.
+__device__ __forceinline__ fp4e2m1x4 cvt_fp32_to_fp4_4x_with_stochastic_rounding(
+    const float2 in01, const float2 in23, const uint32_t rbits) {
+  using namespace nvfp4_b200_detail;
+  return as_fp4x4(rs4(in01.x, in01.y, in23.x, in23.y, rbits));
+}
+
+// in03 / in47: four bf16 each.  rbits03 rounds elements 0-3, rbits47 4-7.
+// Returns eight nibbles, element 0 in bits [3:0].
+template <typename ScaleT>
+__device__ __forceinline__ uint32_t mul_cvt_bf16_to_fp4_8x_stochastic_rounding(
+    const uint64_t in03, const uint64_t in47, const ScaleT scaling_coefficient,
+    const uint32_t rbits03, const uint32_t rbits47) {
+  using namespace nvfp4_b200_detail;
+  static_assert(std::is_same<ScaleT, float>::value || std::is_same<ScaleT, __nv_bfloat16>::value,
+                "scaling coefficient must be float or bf16");
+  float v[8];
+  if constexpr (std::is_same<ScaleT, float>::value) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = bf16_lane(in03, k) * scaling_coefficient;
+      v[k + 4] = bf16_lane(in47, k) * scaling_coefficient;
+    }
+  } else {
+    const float s = __bfloat162float(scaling_coefficient);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = mul_plus_zero(bf16_lane(in03, k), s);
+      v[k + 4] = mul_plus_zero(bf16_lane(in47, k), s);
+    }
+  }
+  const uint32_t lo = rs4(v[0], v[1], v[2], v[3], rbits03);
+  const uint32_t hi = rs4(v[4], v[5], v[6], v[7], rbits47);
+  return lo | (hi << 16);
+}

@@ -1,0 +1,86 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol that
+include/nvfp4_b200.h declares, and rejects bad arguments with the documented
+status codes before touching a GPU (argument checks run first)."""
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "nvfp4_b200.h").read_text()
+    return re.findall(r"NVFP4_API\s+[\w\s\*]+?\b(nvfp4_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "nvfp4_rht_gemm_ntt_w_sfc" in syms and "nvfp4_cvt_fp32_to_fp4_4x_sr" in syms
+    assert len(syms) == len(set(syms))
+
+
+def test_library_exports_every_declared_symbol(nvlib):
+    lib = nvlib.load()
+    from fp4_sm120a_b200._native import SIGNATURES
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+        assert s in SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_status_strings(nvlib):
+    lib = nvlib.load()
+    assert lib.nvfp4_status_string(0) == b"ok"
+    assert b"shape" in lib.nvfp4_status_string(1)
+    assert lib.nvfp4_status_string(99) == b"unknown status"
+
+
+@pytest.mark.parametrize("m,n,k_tile", [(100, 64, 2048), (128, 96, 2048), (-128, 64, 2048),
+                                        (128, 64, 32)])
+def test_rht_rejects_bad_shapes(nvlib, m, n, k_tile):
+    lib = nvlib.load()
+    rc = lib.nvfp4_rht_gemm_ntt_w_sfc(m, n, 16, 16, 16, 16, 16, None, 0, None, k_tile, 0, 0)
+    assert rc == 1
+
+
+def test_rht_zero_size_is_noop(nvlib):
+    lib = nvlib.load()
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc(0, 64, None, None, None, None, None, None, 0, None,
+                                        2048, 0, 0) == 0
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc(128, 0, None, None, None, None, None, None, 0, None,
+                                        2048, 1, 0) == 0
+
+
+def test_rht_rejects_null_and_misaligned(nvlib):
+    lib = nvlib.load()
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc(128, 64, None, 16, 16, 16, 16, None, 0, None, 2048, 0,
+                                        0) == 2
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc(128, 64, 0x1008, 16, 16, 16, 16, None, 0, None, 2048,
+                                        0, 0) == 3
+
+
+def test_sharded_offset_must_align_to_k_tile_chunks(nvlib):
+    lib = nvlib.load()
+    # n_offset = 1024 is not a multiple of the 2048-column chunk
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc_sharded(128, 1024, 16, 16, 16, 16, 16, None, 0, None,
+                                                2048, 1, 0, 1024, 4096) == 1
+    # shard past the end of the problem
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc_sharded(128, 2048, 16, 16, 16, 16, 16, None, 0, None,
+                                                2048, 1, 0, 4096, 4096) == 1
+
+
+def test_batch_entry_points_validate_arguments(nvlib):
+    lib = nvlib.load()
+    assert lib.nvfp4_cvt_fp32_to_fp4_4x_sr(None, None, None, 0, None) == 0
+    assert lib.nvfp4_cvt_fp32_to_fp4_4x_sr(None, 16, 16, 4, None) == 2
+    assert lib.nvfp4_quantize_rowwise_bf16_sr(4, 24, 16, 16, 16, 16, 16, None) == 1
+    assert lib.nvfp4_quantize_rowwise_bf16_sr(4, 32, 0x1008, 16, 16, 16, 16, None) == 3
+    assert lib.nvfp4_amax_bf16(16, 8, None, None) == 2
+
+
+def test_product_path_has_no_oracle_dependency():
+    """The shipped package never imports the oracle (checker only)."""
+    pkg = ROOT / "fp4_sm120a_b200"
+    for p in pkg.rglob("*.py"):
+        t = p.read_text()
+        assert "oracle" not in t.replace("no oracle", ""), p

@@ -1,0 +1,213 @@
+"""CPU tests of the oracle (the C restatement) against published known-answer
+vectors, the reference's own known-answer tests and golden fixtures made by
+running the reference's CPU code (tests/golden/)."""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_philox_known_answers(orc):
+    # Philox4x32-10 known-answer vectors (Salmon et al., SC'11 / Random123):
+    # the counter after init(seed, subseq=0, offset=0) is (0,0,0,0) with key=seed.
+    assert [hex(v) for v in orc.philox(0, 0, 0)] == \
+        ["0x6627e8d5", "0xe169c58d", "0xbc57ac4c", "0x9b00dbd8"]
+
+
+def test_philox_te_counter_layout(orc):
+    # TE's init puts subsequence in (z, w) and offset in (x, y); generate4()
+    # bumps x.  subseq=1 must equal raw counter (0,0,1,0) and skip=1 (0+1) etc.
+    a = orc.philox(7, 3, 5, skip=2)
+    b = orc.philox(7, 3, 7, skip=0)
+    assert (a == b).all()
+    c = orc.philox(7, 3, 0, skip=0)
+    assert not (a == c).all()
+    # carry from x into y: offset 2^32 - 1 then one skip equals offset 2^32
+    assert (orc.philox(1, 0, 2**32 - 1, skip=1) == orc.philox(1, 0, 2**32, skip=0)).all()
+
+
+def test_e2m1_rn_table(orc):
+    # ties go to the even code (stochastic_rounding/sr.sm120.cuh:61-92 relies
+    # on the hardware round-to-nearest-even; test_correctness.cu:43-62).
+    cases = {0.0: 0, 0.25: 0, 0.26: 1, 0.5: 1, 0.75: 2, 1.0: 2, 1.25: 2, 1.3: 3, 1.75: 4,
+             2.5: 4, 2.6: 5, 3.5: 6, 5.0: 6, 5.01: 7, 6.0: 7, 100.0: 7, math.inf: 7}
+    for x, c in cases.items():
+        assert orc.e2m1_rn(x) == c, x
+        assert orc.e2m1_rn(-x) == (c | 8), -x
+    assert orc.e2m1_rn(-0.0) == 8
+
+
+def test_e4m3_codec_roundtrip(orc):
+    # every finite non-negative E4M3 code decodes and re-encodes to itself
+    for code in range(0x7F):
+        v = orc.e4m3_decode(code)
+        assert orc.e4m3(v) == code, code
+    assert orc.e4m3(448.0) == 0x7E and orc.e4m3(1e9) == 0x7E and orc.e4m3(math.inf) == 0x7E
+    assert orc.e4m3(math.nan) == 0x7F
+    assert orc.e4m3(2.0 ** -9) == 1 and orc.e4m3(2.0 ** -10) == 0  # tie to even
+    assert math.isnan(orc.e4m3_decode(0x7F))
+
+
+def test_sr_exact_representables(orc):
+    # stochastic_rounding/sr.software.cu:142-158 and sr.sm120.cu:121-149:
+    # exactly representable values never move, whatever the random bits.
+    reps = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+    for x in reps:
+        for rb in (0, 1, 127, 128, 255):
+            assert orc.e2m1_decode(orc.e2m1_sr(x, rb)) == x
+
+
+def test_sr_saturation(orc):
+    # sr.software.cu:160-176, sr.sm120.cu:149-160: |x| >= 6 saturates to +-6.
+    for x, e in [(7.0, 6.0), (-7.0, -6.0), (math.inf, 6.0), (-math.inf, -6.0), (1000.0, 6.0),
+                 (-1000.0, -6.0)]:
+        for rb in (0, 200, 255):
+            assert orc.e2m1_decode(orc.e2m1_sr(x, rb)) == e
+
+
+def test_sr_probability_matches_bracket(orc):
+    # P(round up) = (|x| - lo) / (hi - lo) over the 256 random bytes
+    # (sr.sm120.cu Tests 1/2 check the same property statistically).
+    for x, lo, hi in [(0.3, 0.0, 0.5), (1.1, 1.0, 1.5), (2.5, 2.0, 3.0), (3.3, 3.0, 4.0),
+                      (5.0, 4.0, 6.0), (0.1, 0.0, 0.5)]:
+        ups = sum(orc.e2m1_decode(orc.e2m1_sr(x, b)) == hi for b in range(256))
+        p = (x - lo) / (hi - lo)
+        assert abs(ups / 256 - p) <= 1.0 / 256 + 1e-6, (x, ups)
+
+
+def test_scale_semantics(orc):
+    # sr.software.cu:183-200: bf16 ones with scale (2, 0.5) -> (2, 0.5, 2, 0.5)
+    ones = np.full(4, 0x3F80, np.uint16)
+    out = orc.mul_cvt_bf16_to_fp4_4x_sr(ones, (2.0, 0.5), np.array([0xABCDEF01], np.uint32))
+    nib = orc.unpack_nibbles(out.view(np.uint8))
+    assert list(orc.e2m1_decode(nib)) == [2.0, 0.5, 2.0, 0.5]
+    # sr.sm120.cu Tests 7-9 scale semantics: fp32 (1,1.5,1,1.5)*(2,2) -> (2,3,2,3)
+    out = orc.mul_cvt_fp32_to_fp4_4x_sr(np.array([1, 1.5, 1, 1.5], np.float32), (2.0, 2.0),
+                                        np.array([0x12345678], np.uint32))
+    assert list(orc.e2m1_decode(orc.unpack_nibbles(out.view(np.uint8)))) == [2, 3, 2, 3]
+
+
+def test_sr_byte_to_element_mapping(orc):
+    # element k is rounded with byte (3 - k) of the word (sr.sm120.cuh:61-71, 98-106):
+    # x = 0.25 rounds up iff byte >= 128.
+    x = np.full(4, 0.25, np.float32)
+    for k in range(4):
+        word = np.array([0x80 << (8 * (3 - k))], np.uint32)
+        nib = orc.unpack_nibbles(orc.cvt_fp32_to_fp4_4x_sr(x, word).view(np.uint8))
+        assert list(orc.e2m1_decode(nib)) == [0.5 if j == k else 0.0 for j in range(4)]
+
+
+def test_8x_bf16_scale_negative_zero(orc):
+    # fma(x, s, +0) turns -0 into +0 (te_ref ptx.cuh:839-870) while the float
+    # scale keeps -0 (ptx.cuh:871-910).
+    xb = np.array([0x8000] + [0x3F80] * 7, np.uint16)   # -0, then ones
+    rb = np.zeros(2, np.uint32)
+    f = orc.mul_cvt_bf16_to_fp4_8x_sr(xb, 1.0, rb, scale_is_bf16=False)
+    b = orc.mul_cvt_bf16_to_fp4_8x_sr(xb, 1.0, rb, scale_is_bf16=True)
+    assert int(f[0]) & 0xF == 0x8 and int(b[0]) & 0xF == 0x0
+
+
+def test_global_encode_scale(orc):
+    # core.inc:3-11
+    assert orc.lib().orc_global_encode_scale(4.0) == pytest.approx(672.0)
+    assert orc.lib().orc_global_encode_scale(0.0) == 1.0
+    assert orc.lib().orc_global_encode_scale(math.inf) == 1.0
+    assert orc.lib().orc_global_encode_scale(1e-45) == pytest.approx(3.4028234663852886e38)
+
+
+def _golden(name):
+    p = GOLDEN / name
+    if not p.exists():
+        pytest.skip(f"fixture {name} not generated")
+    return np.load(p)
+
+
+def test_oracle_vs_reference_naive_rht_fixture(orc):
+    """The reference's NaiveReference (rht_gemm/test_correctness.cu:110-198),
+    run here from its own source, on finite data with amax = 4 (where its
+    S_enc / 6 equals TE's S_enc * (1/6)): bit-exact on FP4 codes and SFC."""
+    g = _golden("ref_naive_rht.npz")
+    for key in [k for k in g.files if k.startswith("A_")]:
+        tag = key[2:]
+        m, n, fm = (int(v) for v in g["shape_" + tag])
+        C, S = orc.rht_gemm_ntt_w_sfc(m, n, g[key], g["B"], float(g["amax_" + tag]),
+                                      sr=False, fast_math=bool(fm))
+        assert (S == g["SFC_" + tag]).all(), tag
+        if fm:
+            # fast math: TE/the device use rcp.approx; NaiveReference and the
+            # oracle use 1/x.  Same SFC, FP4 within one code step.
+            d = np.abs(orc.e2m1_decode(orc.unpack_nibbles(C)) -
+                       orc.e2m1_decode(orc.unpack_nibbles(g["C_" + tag])))
+            assert (d <= 1.0 + 1e-6).all()
+        else:
+            assert (C == g["C_" + tag]).all(), tag
+
+
+def test_oracle_vs_teref_fixture(orc):
+    """TE's SM100 kernel run on a B200 (tests/golden/gen_teref_fixtures.py):
+    bit-exact for RN and SR; FP4 within one step for fast math."""
+    g = _golden("teref_rht.npz")
+    cases = sorted({k.split("__")[0] for k in g.files if "__" in k})
+    assert cases
+    for tag in cases:
+        m, n, sr, fm, ktile = (int(v) for v in g[tag + "__cfg"])
+        rng = g[tag + "__rng"] if sr else None
+        C, S = orc.rht_gemm_ntt_w_sfc(m, n, g[tag + "__A"], g[tag + "__B"],
+                                      float(g[tag + "__amax"][0]), rng_state=rng,
+                                      k_tile_size=ktile, sr=bool(sr), fast_math=bool(fm))
+        if fm:
+            assert (S == g[tag + "__SFC"]).mean() > 0.999, tag
+            d = np.abs(orc.e2m1_decode(orc.unpack_nibbles(C)).astype(np.float64) -
+                       orc.e2m1_decode(orc.unpack_nibbles(g[tag + "__C"])))
+            finite = np.isfinite(d)
+            assert (d[finite] <= 2.0).all(), tag
+        else:
+            assert (S == g[tag + "__SFC"]).all(), tag
+            assert (C == g[tag + "__C"]).all(), tag
+
+
+def test_oracle_vs_teref_sr_functions_fixture(orc):
+    """TE's native cvt.rs functions (te_ref ptx.cuh:563-918) run on a B200."""
+    g = _golden("teref_sr.npz")
+    sc = (float(g["scale"][0]), float(g["scale"][1]))
+    assert (orc.cvt_fp32_to_fp4_4x_sr(g["f32"], g["rb"]) == g["cvt_fp32_4x"]).all()
+    assert (orc.mul_cvt_fp32_to_fp4_4x_sr(g["f32"], sc, g["rb"]) == g["mul_fp32_4x"]).all()
+    assert (orc.mul_cvt_bf16_to_fp4_4x_sr(g["bf16"], sc, g["rb"]) == g["mul_bf16_4x"]).all()
+    assert (orc.mul_cvt_bf16_to_fp4_8x_sr(g["bf16"], sc[0], g["rb"]) == g["bf16_8x"]).all()
+    assert (orc.mul_cvt_bf16_to_fp4_8x_sr(g["bf16"], sc[0], g["rb"], scale_is_bf16=True) ==
+            g["bf16_8x_bfscale"]).all()
+
+
+def test_oracle_codecs_vs_hardware_fixture(orc):
+    """cvt.rn.satfinite.e2m1x2.f32 / e4m3x2.f32 on special and random values,
+    recorded on a B200."""
+    g = _golden("teref_sr.npz")
+    x = g["codec_in"]
+    e2 = np.array([orc.e2m1_rn(float(v)) for v in x], np.uint8)
+    e4 = np.array([orc.e4m3(float(v)) for v in x], np.uint8)
+    assert (e2 == g["codec_e2m1"]).all()
+    assert (e4 == g["codec_e4m3"]).all()
+
+
+def test_oracle_vs_reference_software_sr_statistics(orc):
+    """sr.software.cuh (the timed CPU baseline) is only statistically
+    equivalent to cvt.rs (stochastic_rounding/README.md:37-38): compare means."""
+    from oracle import ref
+    if not ref.cpu_available():
+        pytest.skip("reference CPU library not built")
+    L = ref.cpu()
+    rng = np.random.default_rng(3)
+    n = 1 << 16
+    x = np.repeat(rng.uniform(-6, 6, 16).astype(np.float32), n // 16)
+    rb = rng.integers(0, 2**32, n // 4, dtype=np.uint32)
+    out_sw = np.zeros(n // 4, np.uint16)
+    L.ref_sw_cvt_fp32_to_fp4_4x_sr(x.ctypes.data, rb.ctypes.data, out_sw.ctypes.data, n // 4, 1)
+    out_or = orc.cvt_fp32_to_fp4_4x_sr(x, rb)
+    dsw = orc.e2m1_decode(orc.unpack_nibbles(out_sw.view(np.uint8))).reshape(16, -1).mean(1)
+    dor = orc.e2m1_decode(orc.unpack_nibbles(out_or.view(np.uint8))).reshape(16, -1).mean(1)
+    xv = x.reshape(16, -1)[:, 0]
+    assert np.allclose(dsw, dor, atol=0.05)
+    assert np.allclose(dor, np.clip(xv, -6, 6), atol=0.05)

@@ -1,0 +1,167 @@
+"""GPU parity of the four stochastic-rounding conversions (batch C-ABI forms)
+against the oracle (bit-exact), the reference's native TE functions run on the
+same GPU (bit-exact), and the reference's known-answer tests."""
+import numpy as np
+import pytest
+import torch
+
+from tests.gpu_helpers import dev, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(n_groups, seed=0):
+    rng = np.random.default_rng(seed)
+    f = (rng.standard_normal(4 * n_groups) * 3.0).astype(np.float32)   # BASELINE cfg1
+    specials = np.array([0.0, -0.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 7.0, np.inf,
+                         -np.inf, np.nan, 1e-40, -1e-40, 1e30, -1e30, 5.999, 0.2499], np.float32)
+    f[:specials.size] = specials
+    rb = rng.integers(0, 2**32, 2 * n_groups, dtype=np.uint32)
+    return f, rb
+
+
+@pytest.mark.parametrize("n_groups", [1, 7, 8, 1000, 1 << 18])
+def test_cvt_fp32_4x_vs_oracle(nvlib, orc, n_groups):
+    f, rb = _inputs(n_groups)
+    rb = rb[:n_groups].copy()
+    out = torch.empty(n_groups, dtype=torch.int16, device="cuda")
+    nvlib.cvt_fp32_to_fp4_4x_sr(dev(f), dev(rb), out, n_groups)
+    got = host(out, np.uint16)
+    assert (got == orc.cvt_fp32_to_fp4_4x_sr(f, rb)).all()
+
+
+@pytest.mark.parametrize("scale", [(1.0, 1.0), (0.75, 1.25), (2.0, 0.5)])
+def test_mul_cvt_fp32_4x_vs_oracle(nvlib, orc, scale):
+    n = 4099
+    f, rb = _inputs(n, seed=1)
+    rb = rb[:n].copy()
+    out = torch.empty(n, dtype=torch.int16, device="cuda")
+    nvlib.mul_cvt_fp32_to_fp4_4x_sr(dev(f), scale, dev(rb), out, n)
+    assert (host(out, np.uint16) == orc.mul_cvt_fp32_to_fp4_4x_sr(f, scale, rb)).all()
+
+
+def test_mul_cvt_bf16_4x_exhaustive(nvlib, orc):
+    """Every bf16 bit pattern with every random byte in every lane position
+    (65536 x 256 values): pins cvt.rs against the noise model of
+    stochastic_rounding/sr.sm120.cuh:27-106, including NaN, Inf, subnormals
+    and negative zero."""
+    vals = np.repeat(np.arange(65536, dtype=np.uint16), 256)            # value-major
+    byte = np.tile(np.arange(256, dtype=np.uint32), 65536)
+    n = vals.size // 4
+    # put element k's byte at position (3 - k) of its group's word
+    pos = (3 - (np.arange(vals.size) % 4)).astype(np.uint32)
+    rb = np.zeros(n, np.uint32)
+    np.bitwise_or.at(rb, np.arange(vals.size) // 4, byte << (8 * pos))
+    out = torch.empty(n, dtype=torch.int16, device="cuda")
+    nvlib.mul_cvt_bf16_to_fp4_4x_sr(dev(vals), (1.0, 1.0), dev(rb), out, n)
+    got = host(out, np.uint16)
+    want = orc.mul_cvt_bf16_to_fp4_4x_sr(vals, (1.0, 1.0), rb)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"{bad.size} mismatching groups, first values " \
+        f"{[hex(v) for v in vals[4 * bad[:4]]]}"
+
+
+@pytest.mark.parametrize("scale_is_bf16", [False, True])
+def test_mul_cvt_bf16_8x_vs_oracle(nvlib, orc, scale_is_bf16):
+    rng = np.random.default_rng(5)
+    n = 3001
+    from oracle import oracle
+    xb = oracle.f32_to_bf16((rng.standard_normal(8 * n) * 4).astype(np.float32))
+    xb[:4] = [0x8000, 0x0000, 0x7F80, 0x7FC0]
+    rb = rng.integers(0, 2**32, 2 * n, dtype=np.uint32)
+    out = torch.empty(n, dtype=torch.int32, device="cuda")
+    nvlib.mul_cvt_bf16_to_fp4_8x_sr(dev(xb), 0.8125, dev(rb), out, n, scale_is_bf16=scale_is_bf16)
+    want = orc.mul_cvt_bf16_to_fp4_8x_sr(xb, 0.8125, rb, scale_is_bf16=scale_is_bf16)
+    assert (host(out, np.uint32) == want).all()
+
+
+def test_unaligned_pointers_use_scalar_path(nvlib, orc):
+    n = 333
+    f, rb = _inputs(n + 1, seed=9)
+    df = dev(np.concatenate([np.zeros(1, np.float32), f]))   # 4-byte offset
+    drb = dev(rb[: n + 1].copy())
+    out = torch.zeros(n + 1, dtype=torch.int16, device="cuda")
+    nvlib.cvt_fp32_to_fp4_4x_sr(df[1:], drb[1:], out[1:], n)
+    got = host(out, np.uint16)[1:]
+    assert (got == orc.cvt_fp32_to_fp4_4x_sr(f[: 4 * n], rb[1: n + 1])).all()
+
+
+def test_sr_functions_vs_reference_native(nvlib):
+    """Bit-exact against TE's own cvt.rs functions (te_ref ptx.cuh:563-918)
+    compiled from the reference tree and run on the same GPU."""
+    from oracle import ref
+    if not ref.gpu_available():
+        pytest.skip("reference GPU library not built")
+    L = ref.gpu()
+    n = 1 << 16
+    f, rb = _inputs(n, seed=11)
+    from oracle import oracle
+    bf = oracle.f32_to_bf16(f)
+    df, dbf, drb = dev(f), dev(bf), dev(rb)
+    a = torch.empty(n, dtype=torch.int16, device="cuda")
+    b = torch.empty(n, dtype=torch.int16, device="cuda")
+    nvlib.cvt_fp32_to_fp4_4x_sr(df, drb, a, n)
+    L.teref_cvt_fp32_to_fp4_4x_sr(df.data_ptr(), drb.data_ptr(), b.data_ptr(), n, None)
+    assert torch.equal(a, b)
+    nvlib.mul_cvt_fp32_to_fp4_4x_sr(df, (0.75, 1.25), drb, a, n)
+    L.teref_mul_cvt_fp32_to_fp4_4x_sr(df.data_ptr(), 0.75, 1.25, drb.data_ptr(), b.data_ptr(), n,
+                                      None)
+    assert torch.equal(a, b)
+    nvlib.mul_cvt_bf16_to_fp4_4x_sr(dbf, (0.75, 1.25), drb, a, n)
+    L.teref_mul_cvt_bf16_to_fp4_4x_sr(dbf.data_ptr(), 0.75, 1.25, drb.data_ptr(), b.data_ptr(),
+                                      n, None)
+    assert torch.equal(a, b)
+    a8 = torch.empty(n // 2, dtype=torch.int32, device="cuda")
+    b8 = torch.empty(n // 2, dtype=torch.int32, device="cuda")
+    for bfs in (0, 1):
+        nvlib.mul_cvt_bf16_to_fp4_8x_sr(dbf, 0.75, drb, a8, n // 2, scale_is_bf16=bool(bfs))
+        L.teref_mul_cvt_bf16_to_fp4_8x_sr(dbf.data_ptr(), 0.75, bfs, drb.data_ptr(), b8.data_ptr(),
+                                          n // 2, None)
+        assert torch.equal(a8, b8)
+
+
+def test_sr_known_answers_on_gpu(nvlib, orc):
+    # stochastic_rounding/sr.software.cu:142-200 on the device
+    reps = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0,
+                     -6.0, 7.0, -7.0, np.inf, -np.inf, 1000.0], np.float32)
+    want = np.clip(reps, -6, 6)
+    x = np.repeat(reps, 4)
+    rb = np.full(reps.size, 0x13579BDF, np.uint32)
+    out = torch.empty(reps.size, dtype=torch.int16, device="cuda")
+    nvlib.cvt_fp32_to_fp4_4x_sr(dev(x), dev(rb), out, reps.size)
+    got = orc.e2m1_decode(orc.unpack_nibbles(host(out, np.uint8))).reshape(-1, 4)
+    assert (got == want[:, None]).all()
+
+
+def test_rowwise_quantize_vs_oracle(nvlib, orc):
+    from tests.gpu_helpers import activations
+    rng = np.random.default_rng(17)
+    rows, cols = 64, 512
+    X = activations(rng, rows * cols).reshape(rows, cols)
+    rb = rng.integers(0, 2**32, rows * cols // 4, dtype=np.uint32)
+    amax = orc.amax_bf16(X)
+    C = torch.empty((rows, cols // 2), dtype=torch.uint8, device="cuda")
+    S = torch.empty((rows, cols // 16), dtype=torch.uint8, device="cuda")
+    nvlib.quantize_rowwise_bf16_sr(rows, cols, dev(X), torch.tensor([amax], device="cuda"),
+                                   dev(rb), C, S)
+    wc, ws = orc.quantize_rowwise_8x_sr(X, amax, rb)
+    assert (host(S, np.uint8) == ws).all()
+    assert (host(C, np.uint8) == wc).all()
+
+
+@pytest.mark.parametrize("n", [1, 7, 8, 4097, 1 << 20])
+def test_amax_vs_oracle(nvlib, orc, n):
+    from tests.gpu_helpers import activations
+    rng = np.random.default_rng(n)
+    x = activations(rng, n)
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    nvlib.amax_bf16(dev(x), n, out)
+    assert host(out, np.float32)[0] == np.float32(orc.amax_bf16(x))
+
+
+def test_amax_nan_propagates(nvlib):
+    from oracle import oracle
+    x = oracle.f32_to_bf16(np.array([1.0, -3.0, np.nan, 2.0] * 100, np.float32))
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    nvlib.amax_bf16(dev(x), x.size, out)
+    assert np.isnan(host(out, np.float32)[0])
