@@ -15,7 +15,8 @@ def _inputs(n_groups, seed=0):
     f = (rng.standard_normal(4 * n_groups) * 3.0).astype(np.float32)   # BASELINE cfg1
     specials = np.array([0.0, -0.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 7.0, np.inf,
                          -np.inf, np.nan, 1e-40, -1e-40, 1e30, -1e30, 5.999, 0.2499], np.float32)
-    f[:specials.size] = specials
+    k = min(specials.size, f.size)
+    f[:k] = specials[:k]
     rb = rng.integers(0, 2**32, 2 * n_groups, dtype=np.uint32)
     return f, rb
 
