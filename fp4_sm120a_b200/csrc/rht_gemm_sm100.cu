@@ -64,7 +64,8 @@ constexpr uint32_t kOffSfc = kOffC + 2 * kCTileBytes;
 constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
 constexpr uint32_t kOffBar = kOffB + 512;
 constexpr uint32_t kNumBars = 2 * kStages + 2 * kAccStages + 1;
-constexpr uint32_t kOffMisc = kOffBar + 8 * kNumBars;
+constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
+constexpr uint32_t kOffMisc = kOffTab + 256 * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
 
 // tcgen05 instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B,
@@ -72,12 +73,37 @@ constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
                             ((16u >> 3) << 17) | ((128u >> 4) << 24);
 
+// Unsigned division by a runtime constant d (1 <= d < 2^31) for numerators
+// below 2^31: q = (umulhi(n, mul) + n) >> shift (round-up method of
+// Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994).
+struct FastDiv {
+  uint32_t mul, shift;
+  __host__ __device__ __forceinline__ uint32_t div(uint32_t n) const {
+#if defined(__CUDA_ARCH__)
+    return (__umulhi(n, mul) + n) >> shift;
+#else
+    return (uint32_t)((((uint64_t)n * mul) >> 32) + n) >> shift;
+#endif
+  }
+};
+inline FastDiv make_fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  FastDiv f;
+  f.mul = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+  f.shift = l;
+  return f;
+}
+
 struct Params {
   int m, n;
   int tiles_m;        // m / 128
   int units;          // tiles_m * ceil(n / 256)
   int n_offset;       // column offset of this shard in the full problem
   uint32_t ktm;       // TE's K_TILE_MAX = min(n_total, k_tile_size) / 64
+  FastDiv div_ktm;    // x / ktm
+  FastDiv div_tiles_m;  // x / tiles_m
   int sfc_vec;        // bytes per SFC store: 16, 4 or 1
   const uint16_t* B;
   uint8_t* sfc;
@@ -85,37 +111,74 @@ struct Params {
   const size_t* rng;
 };
 
+// Work units in the persistent schedule: unit u = tm + tiles_m * un covers
+// rows [128 tm, 128 tm + 128) and columns [256 un, 256 un + 256).  Each CTA
+// walks u = blockIdx.x, blockIdx.x + gridDim.x, ... incrementally.
+struct UnitIter {
+  int u, tm, un, step_m, step_n;
+  __device__ __forceinline__ void init(const Params& p) {
+    u = blockIdx.x;
+    un = (int)p.div_tiles_m.div((uint32_t)u);
+    tm = u - un * p.tiles_m;
+    step_n = (int)p.div_tiles_m.div(gridDim.x);
+    step_m = (int)gridDim.x - step_n * p.tiles_m;
+  }
+  __device__ __forceinline__ void next(const Params& p) {
+    u += gridDim.x;
+    tm += step_m;
+    un += step_n;
+    if (tm >= p.tiles_m) { tm -= p.tiles_m; ++un; }
+  }
+};
+
 struct Unit {
   int tm, m0, n0, nsub, nacc;
 };
-__device__ __forceinline__ Unit decode_unit(const Params& p, int u) {
+__device__ __forceinline__ Unit unit_at(const Params& p, const UnitIter& it) {
   Unit t;
-  t.tm = u % p.tiles_m;
-  t.m0 = t.tm * kBM;
-  t.n0 = (u / p.tiles_m) * kUnitN;
+  t.tm = it.tm;
+  t.m0 = it.tm * kBM;
+  t.n0 = it.un * kUnitN;
   const int rem = (p.n - t.n0) / kSubN;
   t.nsub = rem < 4 ? rem : 4;
   t.nacc = (t.nsub + 1) / 2;
   return t;
 }
 
-// Quantize one 16-vector in place: TE epilogue math (core.inc:439-492).
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// (a, b) * (s, s) with one mul.rn.f32x2: the same rounding as two mul.rn.f32.
+__device__ __forceinline__ void mul2(float& a, float& b, float s) {
+  uint64_t x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(y) : "f"(s));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(x) : "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+
+// Quantize one 16-vector in place with TE's epilogue math (core.inc:439-492):
+// optional bf16 round trip, NaN-propagating amax, SFC = E4M3(amax * S_enc/6),
+// scale = min_nanprop(1 / (E4M3^-1(SFC) * S_dec), FLT_MAX) -- looked up in
+// `tab`, which holds that scale for all 256 SFC codes of this launch -- then
+// FP4 E2M1 by cvt.rs (SR) or cvt.rn.  Returns the SFC code.
 template <bool SR, bool FM>
-__device__ __forceinline__ uint32_t quant16(float* x, float enc_mult, float dec, uint4 rb,
+__device__ __forceinline__ uint32_t quant16(float* x, float enc_mult, const float* tab, uint4 rb,
                                             uint32_t& w0, uint32_t& w1) {
   if constexpr (!FM) {
 #pragma unroll
     for (int k = 0; k < 16; k += 2) bf16_round_pair(x[k], x[k + 1]);
   }
-  float am = 0.0f;
+  float am = max3_nan(fabsf(x[0]), fabsf(x[1]), fabsf(x[2]));
 #pragma unroll
-  for (int k = 0; k < 16; ++k) am = fmax_nan(am, fabsf(x[k]));
+  for (int k = 3; k < 15; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
+  am = fmax_nan(am, fabsf(x[15]));
   const uint32_t code = e4m3_encode(am * enc_mult);
-  const float qs = e4m3_decode(code) * dec;
-  float acc = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
-  acc = fmin_nan(acc, 3.402823466e38f);
+  const float acc = tab[code];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = x[k] * acc;
+  for (int k = 0; k < 16; k += 2) mul2(x[k], x[k + 1], acc);
   if constexpr (SR) {
     w0 = (uint32_t)sr_e2m1x4(x[0], x[1], x[2], x[3], rb.x) |
          ((uint32_t)sr_e2m1x4(x[4], x[5], x[6], x[7], rb.y) << 16);
@@ -128,6 +191,29 @@ __device__ __forceinline__ uint32_t quant16(float* x, float enc_mult, float dec,
          (rn_e2m1x2(x[12], x[13]) << 16) | (rn_e2m1x2(x[14], x[15]) << 24);
   }
   return code;
+}
+
+// Philox4x32-10 for two consecutive counters (ctr and ctr + 1 in x with
+// carry), with the key schedule precomputed in k0[r], k1[r].
+__device__ __forceinline__ void philox_pair(uint32_t x, uint32_t y, uint32_t z, uint32_t w,
+                                            const uint32_t (&k0)[10], const uint32_t (&k1)[10],
+                                            uint4& ra, uint4& rb) {
+  uint32_t a0 = x, a1 = y, a2 = z, a3 = w;
+  uint32_t b0 = x + 1u, b1 = y, b2 = z, b3 = w;
+  if (b0 == 0u) { if (++b1 == 0u) { if (++b2 == 0u) ++b3; } }
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t pa0 = (uint64_t)0xD2511F53u * a0, pa1 = (uint64_t)0xCD9E8D57u * a2;
+    const uint64_t pb0 = (uint64_t)0xD2511F53u * b0, pb1 = (uint64_t)0xCD9E8D57u * b2;
+    const uint32_t na0 = (uint32_t)(pa1 >> 32) ^ a1 ^ k0[r];
+    const uint32_t na2 = (uint32_t)(pa0 >> 32) ^ a3 ^ k1[r];
+    const uint32_t nb0 = (uint32_t)(pb1 >> 32) ^ b1 ^ k0[r];
+    const uint32_t nb2 = (uint32_t)(pb0 >> 32) ^ b3 ^ k1[r];
+    a1 = (uint32_t)pa1; a3 = (uint32_t)pa0; a0 = na0; a2 = na2;
+    b1 = (uint32_t)pb1; b3 = (uint32_t)pb0; b0 = nb0; b2 = nb2;
+  }
+  ra = make_uint4(a0, a1, a2, a3);
+  rb = make_uint4(b0, b1, b2, b3);
 }
 
 // Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast.
@@ -176,6 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmC);
   }
+  float* acc_tab = reinterpret_cast<float*>(smem + kOffTab);
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + 256) {
+    // Reciprocal scale of every SFC code for this launch's global amax:
+    // min_nanprop(1 / (E4M3^-1(code) * S_dec), FLT_MAX), accurate or rcp.approx.
+    const uint32_t code = threadIdx.x - 64;
+    const float enc = global_encode_scale(*p.amax);
+    const float qs = e4m3_decode(code) * __fdiv_rn(1.0f, enc);
+    const float r = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
+    acc_tab[code] = fmin_nan(r, 3.402823466e38f);
+  }
   if (warp == 1) {
     // B into shared memory in the canonical no-swizzle MN-major layout:
     // B(n = c, k) at (c % 8) * 2 + (k % 8) * 16 + (c / 8) * 128 + (k / 8) * 256.
@@ -199,8 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const Unit t = decode_unit(p, u);
+      UnitIter it;
+      for (it.init(p); it.u < p.units && ok; it.next(p)) {
+        const Unit t = unit_at(p, it);
         for (int s = 0; s < t.nsub; ++s) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kWaitLimitNs,
                                  kErrTimeoutProducer, &g_device_error_word)) {
@@ -235,8 +332,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t bdesc = umma_smem_desc(sbase + kOffB, 256, 128, 0);
       uint32_t stage = 0, phase = 0, acc = 0, accph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const Unit t = decode_unit(p, u);
+      UnitIter it;
+      for (it.init(p); it.u < p.units && ok; it.next(p)) {
+        const Unit t = unit_at(p, it);
         for (int a = 0; a < t.nacc && ok; ++a) {
           if (!mbar_wait_bounded(acce_bar(acc), accph ^ 1u, abort_flag, kWaitLimitNs,
                                  kErrTimeoutMma, &g_device_error_word)) {
@@ -284,23 +382,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;      // row within the 128-row tile
     const bool leader = (ew == 0 && lane == 0);
 
-    const float enc = global_encode_scale(*p.amax);
-    const float dec = __fdiv_rn(1.0f, enc);
-    const float enc_mult = enc * (1.0f / 6.0f);
-    uint64_t seed = 0, offset = 0;
-    if (SR && p.rng != nullptr) {
-      seed = p.rng[0];
-      offset = p.rng[1];
+    const float enc_mult = global_encode_scale(*p.amax) * (1.0f / 6.0f);
+    uint32_t k0[10], k1[10];
+    uint32_t olo = 0, ohi = 0;
+    if constexpr (SR) {
+      uint64_t seed = 0, offset = 0;
+      if (p.rng != nullptr) {
+        seed = p.rng[0];
+        offset = p.rng[1];
+      }
+#pragma unroll
+      for (int i = 0; i < 10; ++i) {
+        k0[i] = (uint32_t)seed + (uint32_t)i * 0x9E3779B9u;
+        k1[i] = (uint32_t)(seed >> 32) + (uint32_t)i * 0xBB67AE85u;
+      }
+      olo = (uint32_t)offset;
+      ohi = (uint32_t)(offset >> 32);
     }
     const int sfc_row_bytes = p.n / 16;
 
     uint32_t acc = 0, accph = 0, ucount = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++ucount) {
-      const Unit t = decode_unit(p, u);
+    UnitIter it;
+    for (it.init(p); it.u < p.units; it.next(p), ++ucount) {
+      const Unit t = unit_at(p, it);
       const uint32_t buf = ucount & 1u;
       uint8_t* cst = smem + kOffC + buf * kCTileBytes;
       uint8_t* sst = smem + kOffSfc + buf * kSfcTileBytes;
+      // TE's RNG coordinates of this unit's first 64-column k-block
+      // (core.inc:161-166, 470-475): kb / K_TILE_MAX and kb % K_TILE_MAX.
+      const uint32_t kb0 = (uint32_t)((p.n_offset + t.n0) / kSubN);
+      const uint32_t chunk0 = p.div_ktm.div(kb0);
+      const uint32_t kt0 = kb0 - chunk0 * p.ktm;
       for (int a = 0; a < t.nacc && ok; ++a) {
         if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
           ok = false;
@@ -322,21 +435,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         uint4 rb0 = make_uint4(0, 0, 0, 0), rb1 = rb0;
         if constexpr (SR) {
-          // TE: seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
-          // linear_tile = tile_m + tiles_m * (k_block / K_TILE_MAX), one
-          // generate4() per 16 columns of the 64-column k-tile.
-          const uint32_t kb = (uint32_t)((p.n_offset + t.n0) / kSubN) + (uint32_t)blk;
-          const uint32_t chunk = kb / p.ktm;
+          // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
+          // linear_tile = tile_m + tiles_m * chunk; generate4() number
+          // (column % 64) / 16 of that sequence.
+          uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
+          while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
           const uint32_t L = (uint32_t)t.tm + (uint32_t)p.tiles_m * chunk;
-          const uint32_t seq = (uint32_t)r + (kb - chunk * p.ktm) * 256u + L * p.ktm * 256u;
-          Philox ph;
-          ph.init(seed, (uint64_t)seq, offset, (uint32_t)(slice & 1) * 2u);
-          rb0 = ph.generate4();
-          rb1 = ph.generate4();
+          const uint32_t seq = (uint32_t)r + kt * 256u + L * p.ktm * 256u;
+          // counter (offset_lo, offset_hi, seq, 0) advanced by 2 * (slice & 1)
+          uint32_t cx = olo + (uint32_t)(slice & 1) * 2u, cy = ohi, cz = seq, cw = 0;
+          if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
+          philox_pair(cx, cy, cz, cw, k0, k1, rb0, rb1);
         }
         uint32_t w0, w1, w2, w3;
-        const uint32_t s0 = quant16<SR, FM>(v, enc_mult, dec, rb0, w0, w1);
-        const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, dec, rb1, w2, w3);
+        const uint32_t s0 = quant16<SR, FM>(v, enc_mult, acc_tab, rb0, w0, w1);
+        const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, acc_tab, rb1, w2, w3);
         // swizzled (128-byte pattern) FP4 tile row r, 16-byte chunk a*4+slice
         const uint32_t chunk16 = (uint32_t)(a * 4 + slice) ^ (uint32_t)(r & 7);
         *reinterpret_cast<uint4*>(cst + r * 128 + chunk16 * 16) = make_uint4(w0, w1, w2, w3);
@@ -506,6 +619,8 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.units = p.tiles_m * ((n + kUnitN - 1) / kUnitN);
   p.n_offset = n_offset;
   p.ktm = ktm;
+  p.div_ktm = make_fast_div(ktm);
+  p.div_tiles_m = make_fast_div((uint32_t)p.tiles_m);
   const uintptr_t sfc_addr = reinterpret_cast<uintptr_t>(SFC);
   p.sfc_vec = ((n / 16) % 16 == 0 && sfc_addr % 16 == 0) ? 16 : (sfc_addr % 4 == 0 ? 4 : 1);
   p.B = reinterpret_cast<const uint16_t*>(B);
