@@ -240,26 +240,29 @@ def bench_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
 
     import fp4_sm120a_b200 as nv
+    from fp4_sm120a_b200.sharded import ShardedRhtQuantizer, combine_amax
     nv.load()
     m = COLS
     n_total = ROWS
-    n = n_total // ws
+    rng_state = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
+    qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, stochastic_rounding=True,
+                             rng_state=rng_state)
+    n = qz.n
     A = make_shard(torch, rank, n)
     B = nv.hadamard16(torch.where(torch.arange(16) % 3 == 0, -1.0, 1.0), device="cuda")
     C = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
     S = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
     amax = torch.empty(1, dtype=torch.float32, device="cuda")
-    rng_state = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
+        # amax pre-pass -> int32-MAX allreduce of the scalar -> RHT + NVFP4 cast
         nv.amax_bf16(A, m * n, amax, stream)
-        if ws > 1:
-            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+        combine_amax(amax)
         if ev is not None:
             ev[0].record(stream)
-        nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, rank * n, n_total, 0,
-                                      stream, 2048, stochastic_rounding=True)
+        nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, qz.n_offset, n_total,
+                                      0, stream, 2048, stochastic_rounding=True)
         if ev is not None:
             ev[1].record(stream)
 
@@ -307,12 +310,9 @@ def bench_ours(args):
     dA = torch.empty_like(A)
 
     def e2e_step():
+        # the public API end to end: host shard in, FP4 + SFC back to the host
         dA.copy_(hA, non_blocking=True)
-        nv.amax_bf16(dA, m * n, amax, stream)
-        if ws > 1:
-            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
-        nv.rht_gemm_ntt_w_sfc_sharded(m, n, dA, B, C, S, amax, rng_state, rank * n, n_total, 0,
-                                      stream, 2048, stochastic_rounding=True)
+        qz(dA, B, C, S, amax, stream)
         hC.copy_(C, non_blocking=True)
         hS.copy_(S, non_blocking=True)
 
