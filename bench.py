@@ -338,10 +338,11 @@ def bench_ours(args):
         rht_bytes = m * n * BYTES_PER_ELEM + RHT_FIXED_BYTES
         achieved = rht_bytes / (rht_ms * 1e-3) / 1e9
         traffic = None
-        tp = ROOT / "profiles" / "rht_nvfp4_traffic.json"
+        tp = ROOT / "profiles" / "rht_nvfp4_traffic.txt"
         if tp.exists():
-            t = json.loads(tp.read_text())
-            traffic = round(t["dram_bytes_per_element"] * m * n)
+            for line in tp.read_text().splitlines():
+                if line.startswith("dram_bytes_per_element"):
+                    traffic = round(float(line.split("=")[1]) * m * n)
         clocks = sampler.summary() if sampler else {}
         line = {
             "metric": "RHT+NVFP4 quant HBM GB/s (frac of 8 TB/s) and elem/s at 1/2/4/8 B200",
