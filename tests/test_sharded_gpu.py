@@ -1,0 +1,75 @@
+"""Row-sharded quantization on 2 GPUs over NCCL (skipped with fewer GPUs):
+each rank quantizes its column shard after the int32-MAX amax exchange; the
+gathered shards must equal a single-GPU run of the whole matrix bit for bit."""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+        from fp4_sm120a_b200 import ops
+        from fp4_sm120a_b200.sharded import ShardedRhtQuantizer, init_distributed
+        init_distributed("nccl", timeout_s=60)
+        m, n_total = 1024, 8192
+        g = torch.Generator(device="cuda").manual_seed(7)
+        A = (torch.randn(m * n_total, device="cuda", generator=g) * 2).to(torch.bfloat16)
+        B = ops.hadamard16(device="cuda")
+        rs = torch.tensor([99, 3], dtype=torch.int64, device="cuda")
+        qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, rng_state=rs)
+        shard = A[qz.n_offset * m:(qz.n_offset + qz.n) * m]
+        C, S = qz.outputs()
+        amax = qz(shard, B, C, S)
+        Cs = [torch.empty((m, sz // 2), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
+        Ss = [torch.empty((m, sz // 16), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
+        dist.all_gather(Cs, C)
+        dist.all_gather(Ss, S)
+        ok = True
+        if rank == 0:
+            Cf = torch.empty((m, n_total // 2), dtype=torch.uint8, device="cuda")
+            Sf = torch.empty((m, n_total // 16), dtype=torch.uint8, device="cuda")
+            am = torch.empty(1, device="cuda")
+            ops.amax_bf16(A, m * n_total, am)
+            ops.rht_gemm_ntt_w_sfc(m, n_total, A, B, Cf, Sf, am, rs, 0, None, 2048,
+                                   stochastic_rounding=True)
+            ok = (torch.equal(am, amax) and torch.equal(torch.cat(Cs, 1), Cf)
+                  and torch.equal(torch.cat(Ss, 1), Sf))
+        q.put((rank, bool(ok)))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+def test_two_gpu_sharded_equals_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}, res
