@@ -69,6 +69,29 @@ __device__ __forceinline__ typename GroupIO<KIND>::Out convert_group(
 }
 
 constexpr int kGroupsPerThread = 8;
+static_assert(kGroupsPerThread * sizeof(uint16_t) % 16 == 0,
+              "each thread must write whole 16-byte output vectors");
+
+// Small batches: one group per thread with typed (naturally aligned) loads,
+// so that a few hundred thousand groups still spread over every SM.
+template <int KIND>
+__global__ void __launch_bounds__(256) k_sr_batch1(const typename GroupIO<KIND>::In* __restrict__ in,
+                                                   const uint32_t* __restrict__ rbits,
+                                                   typename GroupIO<KIND>::Out* __restrict__ out,
+                                                   size_t ngroups, float sx, float sy) {
+  using IO = GroupIO<KIND>;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < ngroups; g += stride) {
+    uint32_t r[IO::kWords];
+#pragma unroll
+    for (int w = 0; w < IO::kWords; ++w) r[w] = __ldcs(rbits + g * IO::kWords + w);
+    out[g] = convert_group<KIND>(__ldcs(in + g), r, sx, sy);
+  }
+}
+
+// Below this many groups the one-group-per-thread kernel has more parallelism
+// than the vector kernel can use.
+constexpr size_t kSmallBatch = (size_t)1 << 22;
 
 // Each thread converts 8 consecutive groups: inputs, random words and outputs
 // move as 16-byte vectors (the host only launches this when every base
@@ -144,10 +167,17 @@ int launch_sr_batch(const void* in, const uint32_t* rbits, void* out, size_t ngr
   if (int e = device_sm_count(&sms)) return e;
   const bool aligned = ((uintptr_t)in % 16 == 0) && ((uintptr_t)rbits % 16 == 0) &&
                        ((uintptr_t)out % 16 == 0);
-  if (aligned) {
+  if (aligned && ngroups < kSmallBatch) {
+    size_t blocks = (ngroups + 255) / 256;
+    const size_t cap = (size_t)sms * 32;
+    if (blocks > cap) blocks = cap;
+    k_sr_batch1<KIND><<<(unsigned)blocks, 256, 0, stream>>>(
+        reinterpret_cast<const typename IO::In*>(in), rbits,
+        reinterpret_cast<typename IO::Out*>(out), ngroups, sx, sy);
+  } else if (aligned) {
     const size_t nvec = ngroups / kGroupsPerThread;
     size_t blocks = (nvec + 255) / 256;
-    const size_t cap = (size_t)sms * 8;  // 8 resident 256-thread blocks per SM
+    const size_t cap = (size_t)sms * 32;  // enough 256-thread blocks to fill every SM
     if (blocks > cap) blocks = cap;
     if (blocks == 0) blocks = 1;
     k_sr_batch<KIND><<<(unsigned)blocks, 256, 0, stream>>>(
