@@ -415,24 +415,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t chunk0 = p.div_ktm.div(kb0);
       const uint32_t kt0 = kb0 - chunk0 * p.ktm;
       for (int a = 0; a < t.nacc && ok; ++a) {
-        if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const int blk = 2 * a + (slice >> 1);  // 64-column block within the unit
-        const bool valid = blk < t.nsub;
-        float v[32];
-        if (valid) {
-          tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
-          tc_wait_ld();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acce_bar(acc));
-        if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
-        if (!valid) continue;
-
+        // The random words depend only on coordinates, so they are generated
+        // before waiting for the accumulator and overlap that wait.
         uint4 rb0 = make_uint4(0, 0, 0, 0), rb1 = rb0;
         if constexpr (SR) {
           // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
@@ -447,6 +432,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
           philox_pair(cx, cy, cz, cw, k0, k1, rb0, rb1);
         }
+        if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const bool valid = blk < t.nsub;
+        float v[32];
+        if (valid) {
+          tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
+          tc_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar(acc));
+        if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
+        if (!valid) continue;
+
         uint32_t w0, w1, w2, w3;
         const uint32_t s0 = quant16<SR, FM>(v, enc_mult, acc_tab, rb0, w0, w1);
         const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, acc_tab, rb1, w2, w3);
