@@ -216,13 +216,13 @@ __device__ __forceinline__ void philox_pair(uint32_t x, uint32_t y, uint32_t z, 
   rb = make_uint4(b0, b1, b2, b3);
 }
 
-// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast.
+// Warp-uniform bounded wait: every lane polls the barrier (no divergent
+// branch around the wait) and the warp agrees on the verdict with a vote.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
                                           volatile uint32_t* abort_flag, uint32_t err) {
-  uint32_t ok = 0;
-  if ((threadIdx.x & 31) == 0)
-    ok = mbar_wait_bounded(bar, parity, abort_flag, kWaitLimitNs, err, &g_device_error_word);
-  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
+  const bool ok =
+      mbar_wait_bounded(bar, parity, abort_flag, kWaitLimitNs, err, &g_device_error_word);
+  return __all_sync(0xFFFFFFFFu, ok);
 }
 
 template <bool SR, bool FM>
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (uint32_t a = 0; a < kAccStages; ++a) {
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), kEpiWarps);
+      mbar_init(acce_bar(a), kEpiThreads);   // every epilogue thread arrives
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0u;
@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acce_bar(acc));
+        mbar_arrive(acce_bar(acc));
         if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
         if (!valid) continue;
 
