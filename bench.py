@@ -246,7 +246,7 @@ def bench_ours(args):
     n_total = ROWS
     rng_state = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
     qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, stochastic_rounding=True,
-                             rng_state=rng_state)
+                             rng_state=rng_state, exchange=args.exchange)
     n = qz.n
     A = make_shard(torch, rank, n)
     B = nv.hadamard16(torch.where(torch.arange(16) % 3 == 0, -1.0, 1.0), device="cuda")
@@ -256,13 +256,20 @@ def bench_ours(args):
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
-        # amax pre-pass -> int32-MAX allreduce of the scalar -> RHT + NVFP4 cast
+        # amax pre-pass -> exchange of the scalar -> RHT + NVFP4 cast.  With the
+        # peer exchange the cast kernel itself combines the ranks' amax.
         nv.amax_bf16(A, m * n, amax, stream)
-        combine_amax(amax)
+        if qz.peer is None:
+            combine_amax(amax)
         if ev is not None:
             ev[0].record(stream)
-        nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, qz.n_offset, n_total,
-                                      0, stream, 2048, stochastic_rounding=True)
+        if qz.peer is None:
+            nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, qz.n_offset,
+                                          n_total, 0, stream, 2048, stochastic_rounding=True)
+        else:
+            nv.rht_gemm_ntt_w_sfc_sharded_exchange(m, n, A, B, C, S, amax, amax, rng_state,
+                                                   qz.n_offset, n_total, qz.peer, 0, stream,
+                                                   2048, stochastic_rounding=True)
         if ev is not None:
             ev[1].record(stream)
 
@@ -357,7 +364,7 @@ def bench_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 with 0.1% x50 outliers; BASELINE cfg5 shape)",
-            "config": workload_config(ws),
+            "config": dict(workload_config(ws), amax_exchange=(args.exchange if ws > 1 else "none")),
             "elem_per_s": elems_total / (ms_step * 1e-3),
             "frac_of_8TBs": round(value / NOMINAL_HBM_GBS, 4),
             "step_hbm_gbs": round(elems_total * (BYTES_PER_ELEM + 2.0) / (ms_step * 1e-3) / 1e9,
@@ -394,6 +401,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="how ranks combine the amax when --gpus > 1")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

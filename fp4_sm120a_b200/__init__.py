@@ -14,6 +14,8 @@ from .ops import (  # noqa: F401
     quantize_rowwise_bf16_sr,
     rht_gemm_ntt_w_sfc,
     rht_gemm_ntt_w_sfc_sharded,
+    rht_gemm_ntt_w_sfc_sharded_exchange,
+    PeerExchange,
     rht_gemm_ttt_wrapper,
 )
 

@@ -40,6 +40,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                         c_void_p, c_void_p], c_int),
     "nvfp4_amax_bf16": ([c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "nvfp4_device_error": ([POINTER(c_uint32), c_int], c_int),
+    "nvfp4_exchange_create": ([c_int, c_int, POINTER(c_void_p), c_void_p], c_int),
+    "nvfp4_exchange_connect": ([c_void_p, c_void_p], c_int),
+    "nvfp4_exchange_destroy": ([c_void_p], c_int),
+    "nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange": ([c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                                   c_void_p, c_void_p, c_void_p, c_void_p,
+                                                   c_uint32, c_void_p, c_int, c_int, c_int,
+                                                   c_int, c_int, c_void_p], c_int),
 }
 
 _lib = None

@@ -22,6 +22,7 @@ enum DeviceError : uint32_t {
   kErrTimeoutMma = 2,
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
+  kErrTimeoutExchange = 5,
 };
 
 // ---------------------------------------------------------------------------
@@ -201,6 +202,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
       }
     }
   }
+}
+
+// System-scope release store / acquire load of 64 bits (peer-memory flags).
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void fence_barrier_init() {

@@ -107,9 +107,54 @@ struct Params {
   int sfc_vec;        // bytes per SFC store: 16, 4 or 1
   const uint16_t* B;
   uint8_t* sfc;
-  const float* amax;
+  const float* amax;     // global amax, or this rank's amax when world > 1
   const size_t* rng;
+  // Cross-GPU amax exchange over peer memory (world > 1): peers[q] is rank
+  // q's slot array (2 x world 64-bit slots, double-buffered by epoch parity).
+  const unsigned long long* const* peers;
+  int rank, world;
+  uint32_t epoch;
+  float* amax_out;       // receives the combined amax (block 0), may be null
 };
+
+// The global amax of this launch.  With world > 1: block 0 publishes
+// {epoch, bits of this rank's amax} into slot `rank` of every rank's slot
+// array (system-scope release stores over NVLink), then every block polls
+// its own rank's slots until all `world` of them carry this epoch and takes
+// the bitwise max (amax >= 0, so integer order is value order and NaN wins).
+// Slots alternate by epoch parity: a rank can be at most one launch ahead of
+// a peer that is still reading (its next publish needs this rank's next
+// launch, which starts only after this one ends).  The poll gives up after
+// kWaitLimitNs, records kErrTimeoutExchange and returns NaN.
+__device__ __forceinline__ float launch_amax(const Params& p, volatile uint32_t* abort_flag,
+                                             uint64_t limit_ns) {
+  if (p.world <= 1) return *p.amax;
+  const uint32_t par = p.epoch & 1u;
+  if (blockIdx.x == 0) {
+    const uint32_t bits = __float_as_uint(*p.amax);
+    const unsigned long long val = ((unsigned long long)p.epoch << 32) | bits;
+    for (int q = 0; q < p.world; ++q)
+      st_release_sys_u64(const_cast<unsigned long long*>(p.peers[q]) + par * p.world + p.rank, val);
+  }
+  const unsigned long long* mine = p.peers[p.rank] + par * p.world;
+  uint32_t mx = 0;
+  const uint64_t t0 = globaltimer_ns();
+  for (int q = 0; q < p.world; ++q) {
+    unsigned long long v = ld_acquire_sys_u64(mine + q);
+    while ((uint32_t)(v >> 32) != p.epoch) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *abort_flag = 1u;
+        atomicCAS(&g_device_error_word, 0u, (uint32_t)kErrTimeoutExchange);
+        return __uint_as_float(0x7FFFFFFFu);
+      }
+      v = ld_acquire_sys_u64(mine + q);
+    }
+    mx = max(mx, (uint32_t)v);
+  }
+  const float am = __uint_as_float(mx);
+  if (blockIdx.x == 0 && p.amax_out != nullptr) *p.amax_out = am;
+  return am;
+}
 
 // Work units in the persistent schedule: unit u = tm + tiles_m * un covers
 // rows [128 tm, 128 tm + 128) and columns [256 un, 256 un + 256).  Each CTA
@@ -263,15 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmC);
   }
   float* acc_tab = reinterpret_cast<float*>(smem + kOffTab);
-  if (threadIdx.x >= 64 && threadIdx.x < 64 + 256) {
-    // Reciprocal scale of every SFC code for this launch's global amax:
-    // min_nanprop(1 / (E4M3^-1(code) * S_dec), FLT_MAX), accurate or rcp.approx.
-    const uint32_t code = threadIdx.x - 64;
-    const float enc = global_encode_scale(*p.amax);
-    const float qs = e4m3_decode(code) * __fdiv_rn(1.0f, enc);
-    const float r = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
-    acc_tab[code] = fmin_nan(r, 3.402823466e38f);
-  }
+  float* s_amax = reinterpret_cast<float*>(smem + kOffMisc + 8);
   if (warp == 1) {
     // B into shared memory in the canonical no-swizzle MN-major layout:
     // B(n = c, k) at (c % 8) * 2 + (k % 8) * 16 + (c / 8) * 128 + (k / 8) * 256.
@@ -382,7 +419,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;      // row within the 128-row tile
     const bool leader = (ew == 0 && lane == 0);
 
-    const float enc_mult = global_encode_scale(*p.amax) * (1.0f / 6.0f);
+    // The launch's global amax (possibly exchanged with the other GPUs; the
+    // producer and MMA warps already stream in meanwhile), then the
+    // reciprocal scale of every SFC code:
+    // min_nanprop(1 / (E4M3^-1(code) * S_dec), FLT_MAX), accurate or rcp.approx.
+    if (ew == 0 && lane == 0) *s_amax = launch_amax(p, abort_flag, kWaitLimitNs);
+    named_bar_sync(2, kEpiThreads);
+    const float gamax = *s_amax;
+    if (ew * 32 + lane < 256) {
+      const uint32_t code = (uint32_t)(ew * 32 + lane);
+      const float qs = e4m3_decode(code) * __fdiv_rn(1.0f, global_encode_scale(gamax));
+      const float rcp = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
+      acc_tab[code] = fmin_nan(rcp, 3.402823466e38f);
+    }
+    named_bar_sync(2, kEpiThreads);
+    const float enc_mult = global_encode_scale(gamax) * (1.0f / 6.0f);
     uint32_t k0[10], k1[10];
     uint32_t olo = 0, ohi = 0;
     if constexpr (SR) {
@@ -596,7 +647,9 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
 
 int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
                const float* global_amax, const size_t* rng_state, uint32_t sm_count,
-               cudaStream_t stream, int k_tile_size, int sr, int fm, int n_offset, int n_total) {
+               cudaStream_t stream, int k_tile_size, int sr, int fm, int n_offset, int n_total,
+               const unsigned long long* const* ex_peers = nullptr, int ex_rank = 0,
+               int ex_world = 1, uint32_t ex_epoch = 0, float* amax_out = nullptr) {
   if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
@@ -629,6 +682,11 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.sfc = reinterpret_cast<uint8_t*>(SFC);
   p.amax = global_amax;
   p.rng = rng_state;
+  p.peers = ex_peers;
+  p.rank = ex_rank;
+  p.world = ex_peers ? ex_world : 1;
+  p.epoch = ex_epoch;
+  p.amax_out = amax_out;
 
   int grid = sms;
   if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
@@ -740,6 +798,87 @@ NVFP4_API int nvfp4_rht_gemm_ttt(int m, int n, const void* A, const void* B, voi
                                  int stochastic_rounding, int use_fast_math) {
   return nvfp4_rht_gemm_ntt_w_sfc(n, m, A, B, C, SFC, global_amax, rng_state, sm_count, stream,
                                   k_tile_size, stochastic_rounding, use_fast_math);
+}
+
+// ---------------------------------------------------------------------------
+// Cross-GPU amax exchange over peer memory
+// ---------------------------------------------------------------------------
+struct nvfp4_exchange {
+  int rank, world, device;
+  unsigned long long* local;          // this rank's 2 x world slots
+  void* peer[64];                     // every rank's slot array (self = local)
+  unsigned long long** dev_peers;     // the same pointers, in device memory
+  uint32_t epoch;
+};
+
+NVFP4_API int nvfp4_exchange_create(int rank, int world, nvfp4_exchange** out,
+                                    void* ipc_handle_out) {
+  if (!out || !ipc_handle_out || world < 2 || world > 64 || rank < 0 || rank >= world)
+    return NVFP4_ERR_INVALID_ARGUMENT;
+  nvfp4_exchange* ex = new nvfp4_exchange();
+  ex->rank = rank;
+  ex->world = world;
+  ex->epoch = 0;
+  cudaError_t e = cudaGetDevice(&ex->device);
+  if (!e) e = cudaMalloc(&ex->local, 2 * (size_t)world * sizeof(unsigned long long));
+  if (!e) e = cudaMemset(ex->local, 0, 2 * (size_t)world * sizeof(unsigned long long));
+  if (!e) e = cudaMalloc(&ex->dev_peers, (size_t)world * sizeof(void*));
+  if (!e) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle_out), ex->local);
+  if (!e) e = cudaDeviceSynchronize();
+  if (e) {
+    if (ex->local) cudaFree(ex->local);
+    if (ex->dev_peers) cudaFree(ex->dev_peers);
+    delete ex;
+    return nvfp4::cuda_status(e);
+  }
+  for (int q = 0; q < 64; ++q) ex->peer[q] = nullptr;
+  *out = ex;
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_exchange_connect(nvfp4_exchange* ex, const void* all_handles) {
+  if (!ex || !all_handles) return NVFP4_ERR_INVALID_ARGUMENT;
+  const cudaIpcMemHandle_t* h = reinterpret_cast<const cudaIpcMemHandle_t*>(all_handles);
+  for (int q = 0; q < ex->world; ++q) {
+    if (q == ex->rank) {
+      ex->peer[q] = ex->local;
+      continue;
+    }
+    if (cudaError_t e = cudaIpcOpenMemHandle(&ex->peer[q], h[q], cudaIpcMemLazyEnablePeerAccess))
+      return nvfp4::cuda_status(e);
+  }
+  if (cudaError_t e = cudaMemcpy(ex->dev_peers, ex->peer, (size_t)ex->world * sizeof(void*),
+                                 cudaMemcpyHostToDevice))
+    return nvfp4::cuda_status(e);
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_exchange_destroy(nvfp4_exchange* ex) {
+  if (!ex) return NVFP4_OK;
+  cudaDeviceSynchronize();
+  for (int q = 0; q < ex->world; ++q)
+    if (q != ex->rank && ex->peer[q]) cudaIpcCloseMemHandle(ex->peer[q]);
+  cudaFree(ex->dev_peers);
+  cudaFree(ex->local);
+  delete ex;
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(
+    int m, int n, const void* A, const void* B, void* C, void* SFC, const float* local_amax,
+    float* global_amax_out, const size_t* rng_state, uint32_t sm_count, nvfp4_stream_t stream,
+    int k_tile_size, int stochastic_rounding, int use_fast_math, int n_offset, int n_total,
+    nvfp4_exchange* ex) {
+  if (!ex || ex->peer[ex->rank] == nullptr) return NVFP4_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return NVFP4_ERR_INVALID_SHAPE;   // every rank must join the exchange
+  const uint32_t epoch = ex->epoch + 1;   // epochs start at 1: zeroed slots never match
+  const int rc = rht_launch(m, n, A, B, C, SFC, local_amax, rng_state, sm_count,
+                            (cudaStream_t)stream, k_tile_size, stochastic_rounding != 0,
+                            use_fast_math != 0, n_offset, n_total,
+                            const_cast<const unsigned long long* const*>(ex->dev_peers), ex->rank,
+                            ex->world, epoch, global_amax_out);
+  if (rc == NVFP4_OK) ex->epoch = epoch;
+  return rc;
 }
 
 NVFP4_API int nvfp4_device_error(uint32_t* code, int clear) {

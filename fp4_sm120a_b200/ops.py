@@ -60,6 +60,52 @@ def rht_gemm_ntt_w_sfc_sharded(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr,
          int(stochastic_rounding), int(use_fast_math), n_offset, n_total)
 
 
+class PeerExchange:
+    """Handle of the cross-GPU amax exchange over peer memory (one per rank).
+
+    create() allocates this rank's slots and returns its 64-byte CUDA IPC
+    handle; connect() takes every rank's handle in rank order."""
+
+    def __init__(self, rank: int, world: int):
+        import ctypes
+        from ._native import load
+        self._lib = load()
+        self.rank, self.world = rank, world
+        self.ptr = ctypes.c_void_p()
+        self.handle = ctypes.create_string_buffer(64)
+        call("nvfp4_exchange_create", rank, world, ctypes.byref(self.ptr), self.handle)
+
+    def connect(self, handles: list) -> None:
+        import ctypes
+        blob = ctypes.create_string_buffer(b"".join(bytes(h) for h in handles), 64 * self.world)
+        call("nvfp4_exchange_connect", self.ptr, blob)
+
+    def close(self) -> None:
+        if self.ptr:
+            call("nvfp4_exchange_destroy", self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def rht_gemm_ntt_w_sfc_sharded_exchange(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr,
+                                        local_amax: Ptr, global_amax_out: Ptr, rng_state: Ptr,
+                                        n_offset: int, n_total: int, exchange: PeerExchange,
+                                        sm_count: int = 0, stream=None, k_tile_size: int = 2048,
+                                        *, stochastic_rounding: bool = False,
+                                        use_fast_math: bool = False) -> None:
+    """Sharded cast whose kernel also combines every rank's amax over peer
+    memory (no separate collective)."""
+    call("nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange", m, n, _ptr(A), _ptr(B), _ptr(C),
+         _ptr(SFC), _ptr(local_amax), _ptr(global_amax_out), _ptr(rng_state), sm_count,
+         _stream(stream), k_tile_size, int(stochastic_rounding), int(use_fast_math), n_offset,
+         n_total, exchange.ptr)
+
+
 def rht_gemm_ttt_wrapper(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr, global_amax: Ptr,
                          rng_state: Ptr, sm_count: int = 0, stream=None, k_tile_size: int = 1024,
                          *, stochastic_rounding: bool = False,

@@ -75,7 +75,10 @@ class ShardedRhtQuantizer:
 
     def __init__(self, m: int, n_total: int, *, group=None, k_tile_size: int = 2048,
                  stochastic_rounding: bool = True, use_fast_math: bool = False,
-                 rng_state: Optional[torch.Tensor] = None):
+                 rng_state: Optional[torch.Tensor] = None, exchange: str = "nccl"):
+        """exchange: "nccl" -- int32-MAX allreduce of the amax before the cast;
+        "peer" -- the cast kernel itself publishes and combines the amax over
+        NVLink peer memory (every rank needs a non-empty shard)."""
         self.group = group
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -86,6 +89,19 @@ class ShardedRhtQuantizer:
         self.k_tile_size = k_tile_size
         self.sr, self.fm = stochastic_rounding, use_fast_math
         self.rng_state = rng_state
+        self.peer = None
+        world = self.plan.world
+        if exchange == "peer" and world > 1:
+            if min(self.plan.sizes) == 0:
+                raise ValueError("the peer exchange needs a non-empty shard on every rank")
+            from .ops import PeerExchange
+            self.peer = PeerExchange(self.rank, world)
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(self.peer.handle.raw), group=group)
+            self.peer.connect(handles)
+            dist.barrier(group=group)
+        elif exchange not in ("nccl", "peer"):
+            raise ValueError(exchange)
 
     def outputs(self, device="cuda"):
         C = torch.empty((self.m, self.n // 2), dtype=torch.uint8, device=device)
@@ -105,6 +121,13 @@ class ShardedRhtQuantizer:
             ops.amax_bf16(A_shard, self.m * self.n, amax, stream)
         else:
             local_amax_fn(A_shard, amax)
+        if self.peer is not None and cast_fn is None:
+            # one kernel: publish this rank's amax, combine all ranks', cast
+            ops.rht_gemm_ntt_w_sfc_sharded_exchange(
+                self.m, self.n, A_shard, B, C, S, amax, amax, self.rng_state, self.n_offset,
+                self.n_total, self.peer, 0, stream, self.k_tile_size,
+                stochastic_rounding=self.sr, use_fast_math=self.fm)
+            return amax
         combine_amax(amax, self.group)
         if cast_fn is None:
             if self.n > 0:

@@ -80,6 +80,30 @@ NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded(int m, int n, const void* A, cons
                                                int stochastic_rounding, int use_fast_math,
                                                int n_offset, int n_total);
 
+/* Cross-GPU amax exchange over peer memory (NVLink), fused into the cast.
+ * One process per GPU.  Set-up (allocates; not on the hot path):
+ *   nvfp4_exchange_create(rank, world, &ex, handle)  -- 64-byte CUDA IPC handle out
+ *   (all-gather the handles across ranks in rank order)
+ *   nvfp4_exchange_connect(ex, handles)              -- world x 64 bytes
+ *   (barrier across ranks before the first launch)
+ * Then each rank calls nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange with its
+ * own shard's amax; the kernel publishes it to every peer, combines all ranks'
+ * values (NaN-propagating max) and quantizes with the global amax, which it
+ * also writes to global_amax_out (may be NULL, may alias local_amax).  Every
+ * rank must make the same sequence of calls; a rank that does not join makes
+ * the others' kernels give up after 1 s (nvfp4_device_error reports 5).
+ * No reference counterpart: the reference has no multi-GPU path. */
+typedef struct nvfp4_exchange nvfp4_exchange;
+NVFP4_API int nvfp4_exchange_create(int rank, int world, nvfp4_exchange** ex,
+                                    void* ipc_handle_out);
+NVFP4_API int nvfp4_exchange_connect(nvfp4_exchange* ex, const void* all_handles);
+NVFP4_API int nvfp4_exchange_destroy(nvfp4_exchange* ex);
+NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(
+    int m, int n, const void* A, const void* B, void* C, void* SFC, const float* local_amax,
+    float* global_amax_out, const size_t* rng_state, uint32_t sm_count, nvfp4_stream_t stream,
+    int k_tile_size, int stochastic_rounding, int use_fast_math, int n_offset, int n_total,
+    nvfp4_exchange* ex);
+
 /* Fixed-flag entry points with the signature of the reference test's
  * wrappers run_ref / run_ref_fast / run_ref_sr
  * (rht_gemm/test_compare_ref.cu:70-88): k_tile_size = 2048. */

@@ -22,7 +22,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, exchange="nccl", mode="ok"):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -36,10 +36,23 @@ def _worker(rank, world, port, q):
         A = (torch.randn(m * n_total, device="cuda", generator=g) * 2).to(torch.bfloat16)
         B = ops.hadamard16(device="cuda")
         rs = torch.tensor([99, 3], dtype=torch.int64, device="cuda")
-        qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, rng_state=rs)
+        qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, rng_state=rs, exchange=exchange)
         shard = A[qz.n_offset * m:(qz.n_offset + qz.n) * m]
         C, S = qz.outputs()
-        amax = qz(shard, B, C, S)
+        if mode == "dropout":
+            # rank 1 stays out of one step (no kernel of its in flight); rank 0's
+            # kernel must give up waiting for its amax and report it.
+            if rank == 0:
+                qz(shard, B, C, S)
+                torch.cuda.synchronize()
+                q.put((rank, ops.device_error()))
+            else:
+                q.put((rank, "skipped"))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
+        for _ in range(3):      # several steps: epochs advance, slots alternate
+            amax = qz(shard, B, C, S)
         Cs = [torch.empty((m, sz // 2), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
         Ss = [torch.empty((m, sz // 16), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
         dist.all_gather(Cs, C)
@@ -60,16 +73,28 @@ def _worker(rank, world, port, q):
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-def test_two_gpu_sharded_equals_single_gpu():
+def _run(exchange, mode="ok"):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange, mode)) for r in range(2)]
     for p in ps:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))
     for p in ps:
         p.join(timeout=60)
+    return res
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_two_gpu_sharded_equals_single_gpu(exchange):
+    res = _run(exchange)
     assert res == {0: True, 1: True}, res
+
+
+def test_peer_exchange_gives_up_when_a_rank_does_not_join():
+    res = _run("peer", "dropout")
+    assert res[1] == "skipped"
+    assert res[0] == 5, res     # kErrTimeoutExchange, recorded instead of a hang
