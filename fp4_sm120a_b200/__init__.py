@@ -11,6 +11,9 @@ from .ops import (  # noqa: F401
     mul_cvt_bf16_to_fp4_8x_sr,
     mul_cvt_fp32_to_fp4_4x_sr,
     quantize_rht,
+    quantize_rht_fused,
+    quantize_rht_fused_sharded_exchange,
+    fused_workspace,
     quantize_rowwise_bf16_sr,
     rht_gemm_ntt_w_sfc,
     rht_gemm_ntt_w_sfc_sharded,

@@ -40,6 +40,14 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                         c_void_p, c_void_p], c_int),
     "nvfp4_amax_bf16": ([c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "nvfp4_device_error": ([POINTER(c_uint32), c_int], c_int),
+    "nvfp4_fused_workspace_bytes": ([], c_size_t),
+    "nvfp4_quantize_rht_fused": ([c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_uint32, c_void_p, c_int, c_int, c_int, c_void_p],
+                                 c_int),
+    "nvfp4_quantize_rht_fused_sharded_exchange": ([c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                                   c_void_p, c_void_p, c_void_p, c_uint32,
+                                                   c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                                   c_void_p, c_void_p], c_int),
     "nvfp4_exchange_create": ([c_int, c_int, POINTER(c_void_p), c_void_p], c_int),
     "nvfp4_exchange_connect": ([c_void_p, c_void_p], c_int),
     "nvfp4_exchange_destroy": ([c_void_p], c_int),

@@ -23,6 +23,7 @@ enum DeviceError : uint32_t {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
   kErrTimeoutExchange = 5,
+  kErrTimeoutGridBarrier = 6,
 };
 
 // ---------------------------------------------------------------------------
@@ -211,6 +212,12 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 

@@ -63,7 +63,7 @@ constexpr uint32_t kOffC = kOffA + kStages * kStageBytes;
 constexpr uint32_t kOffSfc = kOffC + 2 * kCTileBytes;
 constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
 constexpr uint32_t kOffBar = kOffB + 512;
-constexpr uint32_t kNumBars = 2 * kStages + 2 * kAccStages + 1;
+constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1;
 constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
 constexpr uint32_t kOffMisc = kOffTab + 256 * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
@@ -115,7 +115,14 @@ struct Params {
   int rank, world;
   uint32_t epoch;
   float* amax_out;       // receives the combined amax (block 0), may be null
+  // Fused kernel: grid-barrier workspace, kFusedWsWords 32-bit words:
+  // [0] arrival count, [1] generation, [2] amax bits, [3] unused,
+  // [4 + b] amax bits of block b.  Zeroed once before first use.
+  uint32_t* ws;
 };
+
+constexpr int kMaxFusedCtas = 1024;
+constexpr int kFusedWsWords = 4 + kMaxFusedCtas;
 
 // The global amax of this launch.  With world > 1: block 0 publishes
 // {epoch, bits of this rank's amax} into slot `rank` of every rank's slot
@@ -126,12 +133,12 @@ struct Params {
 // a peer that is still reading (its next publish needs this rank's next
 // launch, which starts only after this one ends).  The poll gives up after
 // kWaitLimitNs, records kErrTimeoutExchange and returns NaN.
-__device__ __forceinline__ float launch_amax(const Params& p, volatile uint32_t* abort_flag,
-                                             uint64_t limit_ns) {
-  if (p.world <= 1) return *p.amax;
+__device__ __forceinline__ float launch_amax(const Params& p, float local,
+                                             volatile uint32_t* abort_flag, uint64_t limit_ns) {
+  if (p.world <= 1) return local;
   const uint32_t par = p.epoch & 1u;
   if (blockIdx.x == 0) {
-    const uint32_t bits = __float_as_uint(*p.amax);
+    const uint32_t bits = __float_as_uint(local);
     const unsigned long long val = ((unsigned long long)p.epoch << 32) | bits;
     for (int q = 0; q < p.world; ++q)
       st_release_sys_u64(const_cast<unsigned long long*>(p.peers[q]) + par * p.world + p.rank, val);
@@ -158,17 +165,33 @@ __device__ __forceinline__ float launch_amax(const Params& p, volatile uint32_t*
 
 // Work units in the persistent schedule: unit u = tm + tiles_m * un covers
 // rows [128 tm, 128 tm + 128) and columns [256 un, 256 un + 256).  Each CTA
-// walks u = blockIdx.x, blockIdx.x + gridDim.x, ... incrementally.
+// owns u = blockIdx.x, blockIdx.x + gridDim.x, ... and walks them forward, or
+// backward (the fused kernel's second pass, so that it first re-reads the
+// tiles its first pass read last, while they are still in L2).
 struct UnitIter {
   int u, tm, un, step_m, step_n;
-  __device__ __forceinline__ void init(const Params& p) {
-    u = blockIdx.x;
-    un = (int)p.div_tiles_m.div((uint32_t)u);
-    tm = u - un * p.tiles_m;
+  bool rev;
+  __device__ __forceinline__ void init(const Params& p, bool reverse = false) {
+    rev = reverse;
     step_n = (int)p.div_tiles_m.div(gridDim.x);
     step_m = (int)gridDim.x - step_n * p.tiles_m;
+    u = blockIdx.x;
+    if (rev && u < p.units) u += ((p.units - 1 - u) / (int)gridDim.x) * (int)gridDim.x;
+    set(p);
+  }
+  __device__ __forceinline__ void set(const Params& p) {
+    un = (int)p.div_tiles_m.div((uint32_t)u);
+    tm = u - un * p.tiles_m;
+  }
+  __device__ __forceinline__ bool valid(const Params& p) const {
+    return rev ? (u >= (int)blockIdx.x && u < p.units) : (u < p.units);
   }
   __device__ __forceinline__ void next(const Params& p) {
+    if (rev) {
+      u -= gridDim.x;
+      if (u >= 0) set(p);
+      return;
+    }
     u += gridDim.x;
     tm += step_m;
     un += step_n;
@@ -270,7 +293,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
   return __all_sync(0xFFFFFFFFu, ok);
 }
 
-template <bool SR, bool FM>
+template <bool SR, bool FM, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmC, const Params p) {
@@ -287,6 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto accf_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + a); };
   auto acce_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + kAccStages + a); };
   const uint32_t drain_bar = bar0 + 8 * (2 * kStages + 2 * kAccStages);
+  // first pass of the fused kernel: its own ring barriers over the same stages
+  auto full1_bar = [&](uint32_t s) { return bar0 + 8 * (2 * kStages + 2 * kAccStages + 1 + s); };
+  auto empty1_bar = [&](uint32_t s) {
+    return bar0 + 8 * (3 * kStages + 2 * kAccStages + 1 + s);
+  };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
 
@@ -300,6 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acce_bar(a), kEpiThreads);   // every epilogue thread arrives
     }
     mbar_init(drain_bar, 1);
+    for (uint32_t st = 0; st < kStages; ++st) {
+      mbar_init(full1_bar(st), 1);
+      mbar_init(empty1_bar(st), kEpiThreads);
+    }
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -332,8 +364,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
+      if constexpr (FUSED) {
+        // First pass: the same tiles, forward, for the epilogue's amax; its
+        // own barriers (full1 / empty1) over the same ring stages.
+        uint32_t st1 = 0, ph1 = 0, n1 = 0;
+        UnitIter it1;
+        for (it1.init(p); it1.valid(p) && ok; it1.next(p)) {
+          const Unit t = unit_at(p, it1);
+          for (int s = 0; s < t.nsub; ++s) {
+            if (!mbar_wait_bounded(empty1_bar(st1), ph1 ^ 1u, abort_flag, kWaitLimitNs,
+                                   kErrTimeoutProducer, &g_device_error_word)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full1_bar(st1), kStageBytes);
+            const uint32_t dst = sbase + kOffA + st1 * kStageBytes;
+            const int y = t.n0 + s * kSubN;
+            tma_load_2d(dst, &tmA, full1_bar(st1), t.m0, y);
+            tma_load_2d(dst + kHalfBytes, &tmA, full1_bar(st1), t.m0 + 64, y);
+            ++n1;
+            if (++st1 == kStages) { st1 = 0; ph1 ^= 1u; }
+          }
+        }
+        // Every first-pass load lands (bounded, whatever happened), then the
+        // second pass reuses a stage only after the epilogue has read it.
+        const uint32_t pend = n1 < (uint32_t)kStages ? n1 : (uint32_t)kStages;
+        volatile uint32_t never = 0u;
+        for (uint32_t i = 0; i < pend; ++i) {
+          if (st1 == 0) { st1 = kStages - 1; ph1 ^= 1u; } else { --st1; }
+          mbar_wait_bounded(full1_bar(st1), ph1, &never, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
+          if (ok && !mbar_wait_bounded(empty1_bar(st1), ph1, abort_flag, kWaitLimitNs,
+                                       kErrTimeoutProducer, &g_device_error_word))
+            ok = false;
+        }
+      }
       UnitIter it;
-      for (it.init(p); it.u < p.units && ok; it.next(p)) {
+      for (it.init(p, FUSED); it.valid(p) && ok; it.next(p)) {
         const Unit t = unit_at(p, it);
         for (int s = 0; s < t.nsub; ++s) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kWaitLimitNs,
@@ -370,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0, acc = 0, accph = 0;
       bool ok = true;
       UnitIter it;
-      for (it.init(p); it.u < p.units && ok; it.next(p)) {
+      for (it.init(p, FUSED); it.valid(p) && ok; it.next(p)) {
         const Unit t = unit_at(p, it);
         for (int a = 0; a < t.nacc && ok; ++a) {
           if (!mbar_wait_bounded(acce_bar(acc), accph ^ 1u, abort_flag, kWaitLimitNs,
@@ -423,7 +490,70 @@ __global__ void __launch_bounds__(kThreads, 1)
     // producer and MMA warps already stream in meanwhile), then the
     // reciprocal scale of every SFC code:
     // min_nanprop(1 / (E4M3^-1(code) * S_dec), FLT_MAX), accurate or rcp.approx.
-    if (ew == 0 && lane == 0) *s_amax = launch_amax(p, abort_flag, kWaitLimitNs);
+    if constexpr (FUSED) {
+      // First pass: NaN-propagating max of |A| over this CTA's tiles as they
+      // stream through the ring (unsigned max of the bf16 magnitude bits),
+      // then a grid barrier on the workspace combines the CTAs.
+      uint32_t gen = 0;
+      if (leader) gen = ld_acquire_gpu_u32(p.ws + 1);   // before this block arrives
+      uint32_t m2 = 0, st1 = 0, ph1 = 0;
+      bool ok1 = true;
+      const int tid = ew * 32 + lane;                   // 32 bytes of each 16 KiB stage
+      UnitIter it1;
+      for (it1.init(p); it1.valid(p) && ok1; it1.next(p)) {
+        const Unit t = unit_at(p, it1);
+        for (int s = 0; s < t.nsub; ++s) {
+          if (!warp_wait(full1_bar(st1), ph1, abort_flag, kErrTimeoutEpilogue)) {
+            ok1 = false;
+            break;
+          }
+          const uint4* src =
+              reinterpret_cast<const uint4*>(smem + kOffA + st1 * kStageBytes) + 2 * tid;
+          const uint4 x = src[0], y = src[1];
+          m2 = __vmaxu2(m2, x.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.y & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, x.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.w & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, y.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.y & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, y.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.w & 0x7FFF7FFFu);
+          mbar_arrive(empty1_bar(st1));
+          if (++st1 == kStages) { st1 = 0; ph1 ^= 1u; }
+        }
+      }
+      const uint32_t mw = __reduce_max_sync(0xFFFFFFFFu, max(m2 & 0xFFFFu, m2 >> 16));
+      uint32_t* red = reinterpret_cast<uint32_t*>(acc_tab);   // free until the table is built
+      if (lane == 0) red[ew] = mw;
+      named_bar_sync(2, kEpiThreads);
+      if (leader) {
+        uint32_t cta = 0;
+        for (int w = 0; w < kEpiWarps; ++w) cta = max(cta, red[w]);
+        volatile uint32_t* ws = p.ws;
+        ws[4 + blockIdx.x] = cta << 16;                    // this block's amax as fp32 bits
+        __threadfence();
+        if (atomicAdd(p.ws, 1u) == gridDim.x - 1) {
+          uint32_t mx = 0;
+          for (uint32_t b = 0; b < gridDim.x; ++b) mx = max(mx, ws[4 + b]);
+          ws[2] = mx;
+          ws[0] = 0u;                                      // ready for the next launch
+          __threadfence();
+          atomicAdd(p.ws + 1, 1u);                         // release the grid
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_gpu_u32(p.ws + 1) == gen) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs || *abort_flag) {
+              *abort_flag = 1u;
+              atomicCAS(&g_device_error_word, 0u, (uint32_t)kErrTimeoutGridBarrier);
+              break;
+            }
+          }
+        }
+        __threadfence();
+        const float local = __uint_as_float(ws[2]);
+        const float g = launch_amax(p, local, abort_flag, kWaitLimitNs);
+        if (p.world <= 1 && blockIdx.x == 0 && p.amax_out != nullptr) *p.amax_out = g;
+        *s_amax = g;
+      }
+    } else {
+      if (leader) *s_amax = launch_amax(p, *p.amax, abort_flag, kWaitLimitNs);
+    }
     named_bar_sync(2, kEpiThreads);
     const float gamax = *s_amax;
     if (ew * 32 + lane < 256) {
@@ -455,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc = 0, accph = 0, ucount = 0;
     bool ok = true;
     UnitIter it;
-    for (it.init(p); it.u < p.units; it.next(p), ++ucount) {
+    for (it.init(p, FUSED); it.valid(p); it.next(p), ++ucount) {
       const Unit t = unit_at(p, it);
       const uint32_t buf = ucount & 1u;
       uint8_t* cst = smem + kOffC + buf * kCTileBytes;
@@ -628,20 +758,37 @@ int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* o
   return NVFP4_OK;
 }
 
-template <bool SR, bool FM>
+template <bool SR, bool FM, bool FUSED>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p, int grid,
                   cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM>,
+    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM, FUSED>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemBytes))
       return cuda_status(e);
     attr_set[dev] = true;
   }
-  rht_nvfp4_kernel<SR, FM><<<grid, kThreads, kSmemBytes, stream>>>(ta, tc, p);
+  if constexpr (!FUSED) {
+    rht_nvfp4_kernel<SR, FM, FUSED><<<grid, kThreads, kSmemBytes, stream>>>(ta, tc, p);
+  } else {
+    // The fused kernel's blocks meet at a grid barrier: a cooperative launch
+    // guarantees they are all resident (one per SM).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, p))
+      return cuda_status(e);
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -649,7 +796,8 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
                const float* global_amax, const size_t* rng_state, uint32_t sm_count,
                cudaStream_t stream, int k_tile_size, int sr, int fm, int n_offset, int n_total,
                const unsigned long long* const* ex_peers = nullptr, int ex_rank = 0,
-               int ex_world = 1, uint32_t ex_epoch = 0, float* amax_out = nullptr) {
+               int ex_world = 1, uint32_t ex_epoch = 0, float* amax_out = nullptr,
+               uint32_t* fused_ws = nullptr) {
   if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
@@ -658,7 +806,9 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   const int kt = n_total < k_tile_size ? n_total : k_tile_size;
   const uint32_t ktm = (uint32_t)(kt / 64);
   if (n_offset % (int)(ktm * 64) != 0) return NVFP4_ERR_INVALID_SHAPE;
-  if (!A || !B || !C || !SFC || !global_amax) return NVFP4_ERR_INVALID_ARGUMENT;
+  const bool fused = fused_ws != nullptr;
+  if (!A || !B || !C || !SFC || (!global_amax && !fused)) return NVFP4_ERR_INVALID_ARGUMENT;
+  if (fused && (uintptr_t)fused_ws % 4) return NVFP4_ERR_MISALIGNED;
   if ((uintptr_t)A % 16 || (uintptr_t)C % 16 || (uintptr_t)B % 2) return NVFP4_ERR_MISALIGNED;
   int sms = 0;
   if (int e = device_sm_count(&sms)) return e;
@@ -687,15 +837,23 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.world = ex_peers ? ex_world : 1;
   p.epoch = ex_epoch;
   p.amax_out = amax_out;
+  p.ws = fused_ws;
 
   int grid = sms;
   if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
   if (p.units < grid) grid = p.units;
 
-  if (sr && fm) return launch_kernel<true, true>(ta, tc, p, grid, stream);
-  if (sr) return launch_kernel<true, false>(ta, tc, p, grid, stream);
-  if (fm) return launch_kernel<false, true>(ta, tc, p, grid, stream);
-  return launch_kernel<false, false>(ta, tc, p, grid, stream);
+  if (fused) {
+    if (grid > kMaxFusedCtas) grid = kMaxFusedCtas;
+    if (sr && fm) return launch_kernel<true, true, true>(ta, tc, p, grid, stream);
+    if (sr) return launch_kernel<true, false, true>(ta, tc, p, grid, stream);
+    if (fm) return launch_kernel<false, true, true>(ta, tc, p, grid, stream);
+    return launch_kernel<false, false, true>(ta, tc, p, grid, stream);
+  }
+  if (sr && fm) return launch_kernel<true, true, false>(ta, tc, p, grid, stream);
+  if (sr) return launch_kernel<true, false, false>(ta, tc, p, grid, stream);
+  if (fm) return launch_kernel<false, true, false>(ta, tc, p, grid, stream);
+  return launch_kernel<false, false, false>(ta, tc, p, grid, stream);
 }
 
 }  // namespace rht
@@ -877,6 +1035,38 @@ NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(
                             use_fast_math != 0, n_offset, n_total,
                             const_cast<const unsigned long long* const*>(ex->dev_peers), ex->rank,
                             ex->world, epoch, global_amax_out);
+  if (rc == NVFP4_OK) ex->epoch = epoch;
+  return rc;
+}
+
+NVFP4_API size_t nvfp4_fused_workspace_bytes(void) {
+  return (size_t)nvfp4::rht::kFusedWsWords * sizeof(uint32_t);
+}
+
+NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* B, void* C,
+                                       void* SFC, float* amax_out, const size_t* rng_state,
+                                       uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
+                                       int stochastic_rounding, int use_fast_math,
+                                       void* workspace) {
+  if (!workspace) return NVFP4_ERR_INVALID_ARGUMENT;
+  return rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count, (cudaStream_t)stream,
+                    k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n, nullptr, 0,
+                    1, 0, amax_out, reinterpret_cast<uint32_t*>(workspace));
+}
+
+NVFP4_API int nvfp4_quantize_rht_fused_sharded_exchange(
+    int m, int n, const void* A, const void* B, void* C, void* SFC, float* amax_out,
+    const size_t* rng_state, uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
+    int stochastic_rounding, int use_fast_math, int n_offset, int n_total, nvfp4_exchange* ex,
+    void* workspace) {
+  if (!ex || ex->peer[ex->rank] == nullptr || !workspace) return NVFP4_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return NVFP4_ERR_INVALID_SHAPE;   // every rank must join the exchange
+  const uint32_t epoch = ex->epoch + 1;
+  const int rc = rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count,
+                            (cudaStream_t)stream, k_tile_size, stochastic_rounding != 0,
+                            use_fast_math != 0, n_offset, n_total,
+                            const_cast<const unsigned long long* const*>(ex->dev_peers), ex->rank,
+                            ex->world, epoch, amax_out, reinterpret_cast<uint32_t*>(workspace));
   if (rc == NVFP4_OK) ex->epoch = epoch;
   return rc;
 }

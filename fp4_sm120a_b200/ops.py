@@ -106,6 +106,36 @@ def rht_gemm_ntt_w_sfc_sharded_exchange(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, 
          n_total, exchange.ptr)
 
 
+def fused_workspace(device="cuda") -> torch.Tensor:
+    """Zeroed workspace for the fused amax + cast kernel (one per concurrent
+    stream of fused launches)."""
+    from ._native import load
+    return torch.zeros(load().nvfp4_fused_workspace_bytes(), dtype=torch.uint8, device=device)
+
+
+def quantize_rht_fused(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr, amax_out: Ptr,
+                       rng_state: Ptr, workspace: Ptr, sm_count: int = 0, stream=None,
+                       k_tile_size: int = 2048, *, stochastic_rounding: bool = False,
+                       use_fast_math: bool = False) -> None:
+    """Global amax of A and the RHT + NVFP4 cast in one kernel (results equal
+    amax_bf16 followed by rht_gemm_ntt_w_sfc)."""
+    call("nvfp4_quantize_rht_fused", m, n, _ptr(A), _ptr(B), _ptr(C), _ptr(SFC), _ptr(amax_out),
+         _ptr(rng_state), sm_count, _stream(stream), k_tile_size, int(stochastic_rounding),
+         int(use_fast_math), _ptr(workspace))
+
+
+def quantize_rht_fused_sharded_exchange(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr,
+                                        amax_out: Ptr, rng_state: Ptr, n_offset: int,
+                                        n_total: int, exchange: "PeerExchange", workspace: Ptr,
+                                        sm_count: int = 0, stream=None, k_tile_size: int = 2048,
+                                        *, stochastic_rounding: bool = False,
+                                        use_fast_math: bool = False) -> None:
+    call("nvfp4_quantize_rht_fused_sharded_exchange", m, n, _ptr(A), _ptr(B), _ptr(C),
+         _ptr(SFC), _ptr(amax_out), _ptr(rng_state), sm_count, _stream(stream), k_tile_size,
+         int(stochastic_rounding), int(use_fast_math), n_offset, n_total, exchange.ptr,
+         _ptr(workspace))
+
+
 def rht_gemm_ttt_wrapper(m: int, n: int, A: Ptr, B: Ptr, C: Ptr, SFC: Ptr, global_amax: Ptr,
                          rng_state: Ptr, sm_count: int = 0, stream=None, k_tile_size: int = 1024,
                          *, stochastic_rounding: bool = False,

@@ -35,6 +35,25 @@ def _case(a, g):
             ops.rht_gemm_ntt_w_sfc(a.m, a.n, A, B, C, S, am, rs, 0, None, 2048,
                                    stochastic_rounding=bool(a.sr), use_fast_math=bool(a.fm))
         return f, a.m * a.n * 2.5625 + 516, a.m * a.n
+    if a.kernel in ("fused", "twostep"):
+        # amax + cast: one fused launch, or the amax pre-pass then the cast
+        A = torch.randn(a.m * a.n, device="cuda", generator=g).to(torch.bfloat16)
+        B = ops.hadamard16(device="cuda")
+        C = torch.empty(a.m * a.n // 2, dtype=torch.uint8, device="cuda")
+        S = torch.empty(a.m * a.n // 16, dtype=torch.uint8, device="cuda")
+        am = torch.empty(1, device="cuda")
+        rs = torch.tensor([1, 0], dtype=torch.int64, device="cuda")
+        ws = ops.fused_workspace()
+
+        def f():
+            if a.kernel == "fused":
+                ops.quantize_rht_fused(a.m, a.n, A, B, C, S, am, rs, ws, 0, None, 2048,
+                                       stochastic_rounding=bool(a.sr), use_fast_math=bool(a.fm))
+            else:
+                ops.amax_bf16(A, a.m * a.n, am)
+                ops.rht_gemm_ntt_w_sfc(a.m, a.n, A, B, C, S, am, rs, 0, None, 2048,
+                                       stochastic_rounding=bool(a.sr), use_fast_math=bool(a.fm))
+        return f, a.m * a.n * 2.5625 + 516, a.m * a.n
     if a.kernel == "amax":
         n = a.m * a.n
         A = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
@@ -63,7 +82,7 @@ def _case(a, g):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["rht", "amax", "sr", "rowwise"])
+    ap.add_argument("kernel", choices=["rht", "amax", "sr", "rowwise", "fused", "twostep"])
     ap.add_argument("--m", type=int, default=14336)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--sr", type=int, default=1)

@@ -75,10 +75,13 @@ class ShardedRhtQuantizer:
 
     def __init__(self, m: int, n_total: int, *, group=None, k_tile_size: int = 2048,
                  stochastic_rounding: bool = True, use_fast_math: bool = False,
-                 rng_state: Optional[torch.Tensor] = None, exchange: str = "nccl"):
+                 rng_state: Optional[torch.Tensor] = None, exchange: str = "nccl",
+                 fused: bool = False):
         """exchange: "nccl" -- int32-MAX allreduce of the amax before the cast;
         "peer" -- the cast kernel itself publishes and combines the amax over
-        NVLink peer memory (every rank needs a non-empty shard)."""
+        NVLink peer memory (every rank needs a non-empty shard).
+        fused: one kernel computes the shard's amax and casts (single GPU, or
+        with exchange="peer")."""
         self.group = group
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -90,7 +93,12 @@ class ShardedRhtQuantizer:
         self.sr, self.fm = stochastic_rounding, use_fast_math
         self.rng_state = rng_state
         self.peer = None
+        self.fused = fused
+        self.workspace = None
         world = self.plan.world
+        if fused and world > 1 and exchange != "peer":
+            raise ValueError("the fused kernel combines the ranks' amax over peer memory; "
+                             "use exchange='peer'")
         if exchange == "peer" and world > 1:
             if min(self.plan.sizes) == 0:
                 raise ValueError("the peer exchange needs a non-empty shard on every rank")
@@ -117,6 +125,19 @@ class ShardedRhtQuantizer:
         from . import ops
         if amax is None:
             amax = torch.empty(1, dtype=torch.float32, device=A_shard.device)
+        if self.fused and cast_fn is None and local_amax_fn is None:
+            if self.workspace is None:
+                self.workspace = ops.fused_workspace(A_shard.device)
+            if self.peer is not None:
+                ops.quantize_rht_fused_sharded_exchange(
+                    self.m, self.n, A_shard, B, C, S, amax, self.rng_state, self.n_offset,
+                    self.n_total, self.peer, self.workspace, 0, stream, self.k_tile_size,
+                    stochastic_rounding=self.sr, use_fast_math=self.fm)
+            else:   # one rank: the shard is the whole matrix
+                ops.quantize_rht_fused(self.m, self.n, A_shard, B, C, S, amax, self.rng_state,
+                                       self.workspace, 0, stream, self.k_tile_size,
+                                       stochastic_rounding=self.sr, use_fast_math=self.fm)
+            return amax
         if local_amax_fn is None:
             ops.amax_bf16(A_shard, self.m * self.n, amax, stream)
         else:

@@ -104,6 +104,31 @@ NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(
     int k_tile_size, int stochastic_rounding, int use_fast_math, int n_offset, int n_total,
     nvfp4_exchange* ex);
 
+/* Global amax and cast in ONE kernel (no separate pre-pass): a first pass
+ * streams A through the kernel's TMA ring to take the NaN-propagating max of
+ * |A|, the blocks meet at a grid barrier (cooperative launch, one block per
+ * SM), and the cast then walks its tiles in reverse so that the tiles read
+ * last are re-read from L2.  Writes the amax to *amax_out (device float, may
+ * be NULL).  Results equal nvfp4_amax_bf16 followed by
+ * nvfp4_rht_gemm_ntt_w_sfc.  `workspace` is nvfp4_fused_workspace_bytes()
+ * bytes of device memory, zeroed once before first use, never used by two
+ * launches at the same time; each launch leaves it ready for the next.
+ * No reference counterpart: the reference takes the amax as an input and has
+ * no amax kernel; this is the fused form its callers would otherwise need. */
+NVFP4_API size_t nvfp4_fused_workspace_bytes(void);
+NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* B, void* C,
+                                       void* SFC, float* amax_out, const size_t* rng_state,
+                                       uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
+                                       int stochastic_rounding, int use_fast_math,
+                                       void* workspace);
+/* The same for one rank's column shard; the kernel also combines the ranks'
+ * amax over peer memory (see nvfp4_exchange_create). */
+NVFP4_API int nvfp4_quantize_rht_fused_sharded_exchange(
+    int m, int n, const void* A, const void* B, void* C, void* SFC, float* amax_out,
+    const size_t* rng_state, uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
+    int stochastic_rounding, int use_fast_math, int n_offset, int n_total, nvfp4_exchange* ex,
+    void* workspace);
+
 /* Fixed-flag entry points with the signature of the reference test's
  * wrappers run_ref / run_ref_fast / run_ref_sr
  * (rht_gemm/test_compare_ref.cu:70-88): k_tile_size = 2048. */

@@ -22,7 +22,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q, exchange="nccl", mode="ok"):
+def _worker(rank, world, port, q, exchange="nccl", mode="ok", fused=False):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -36,7 +36,8 @@ def _worker(rank, world, port, q, exchange="nccl", mode="ok"):
         A = (torch.randn(m * n_total, device="cuda", generator=g) * 2).to(torch.bfloat16)
         B = ops.hadamard16(device="cuda")
         rs = torch.tensor([99, 3], dtype=torch.int64, device="cuda")
-        qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, rng_state=rs, exchange=exchange)
+        qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, rng_state=rs, exchange=exchange,
+                                 fused=fused)
         shard = A[qz.n_offset * m:(qz.n_offset + qz.n) * m]
         C, S = qz.outputs()
         if mode == "dropout":
@@ -73,13 +74,13 @@ def _worker(rank, world, port, q, exchange="nccl", mode="ok"):
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-def _run(exchange, mode="ok"):
+def _run(exchange, mode="ok", fused=False):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange, mode)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange, mode, fused)) for r in range(2)]
     for p in ps:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))
@@ -88,9 +89,9 @@ def _run(exchange, mode="ok"):
     return res
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
-def test_two_gpu_sharded_equals_single_gpu(exchange):
-    res = _run(exchange)
+@pytest.mark.parametrize("exchange,fused", [("nccl", False), ("peer", False), ("peer", True)])
+def test_two_gpu_sharded_equals_single_gpu(exchange, fused):
+    res = _run(exchange, fused=fused)
     assert res == {0: True, 1: True}, res
 
 
