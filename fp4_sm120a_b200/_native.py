@@ -44,6 +44,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_quantize_rht_fused": ([c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_uint32, c_void_p, c_int, c_int, c_int, c_void_p],
                                  c_int),
+    "nvfp4_quantize_rht_fused_noalloc": ([c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_uint32, c_void_p, c_int, c_int,
+                                          c_int], c_int),
     "nvfp4_quantize_rht_fused_sharded_exchange": ([c_int, c_int, c_void_p, c_void_p, c_void_p,
                                                    c_void_p, c_void_p, c_void_p, c_uint32,
                                                    c_void_p, c_int, c_int, c_int, c_int, c_int,

@@ -906,6 +906,8 @@ NVFP4_API const char* nvfp4_status_string(int status) {
     case NVFP4_ERR_CUDA: return "CUDA runtime error";
     case NVFP4_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs compute capability 10.0)";
     case NVFP4_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out";
+    case NVFP4_ERR_SCRATCH_CAPACITY:
+      return "launch needs more blocks than the static scratch of the no-allocation entry holds";
     default: return "unknown status";
   }
 }
@@ -1052,6 +1054,58 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
   return rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count, (cudaStream_t)stream,
                     k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n, nullptr, 0,
                     1, 0, amax_out, reinterpret_cast<uint32_t*>(workspace));
+}
+
+// ---------------------------------------------------------------------------
+// Fused amax + cast without any allocation by the caller or the library.
+// The grid-barrier workspace lives in this static device array (kFusedWsWords
+// 32-bit words, 4112 bytes, on every GPU that loads the library, until the
+// process exits).  Host code must not hand the array's name to a kernel:
+// there it only stands for the symbol, so its device address is looked up
+// once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+namespace {
+static __device__ __align__(256) uint32_t g_fused_scratch[nvfp4::rht::kFusedWsWords];
+
+// Device address of g_fused_scratch on the current device (looked up on the
+// first call per device).
+int fused_scratch_address(uint32_t** out) {
+  static std::mutex mu;
+  static uint32_t* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return nvfp4::cuda_status(e);
+  if (dev >= 64) return NVFP4_ERR_UNSUPPORTED_DEVICE;
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaError_t e = cudaGetSymbolAddress(&ptr, g_fused_scratch)) return nvfp4::cuda_status(e);
+    addr[dev] = reinterpret_cast<uint32_t*>(ptr);
+  }
+  *out = addr[dev];
+  return NVFP4_OK;
+}
+}  // namespace
+
+NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, const void* B,
+                                               void* C, void* SFC, float* amax_out,
+                                               const size_t* rng_state, uint32_t sm_count,
+                                               nvfp4_stream_t stream, int k_tile_size,
+                                               int stochastic_rounding, int use_fast_math) {
+  // The static scratch holds one partial amax per block, for at most
+  // kMaxFusedCtas blocks; a launch that would need more is refused.
+  int sms = 0;
+  if (int e = nvfp4::device_sm_count(&sms)) return e;
+  const int want = (sm_count > 0 && (int)sm_count < sms) ? (int)sm_count : sms;
+  if (want > nvfp4::rht::kMaxFusedCtas) return NVFP4_ERR_SCRATCH_CAPACITY;
+  uint32_t* scratch = nullptr;
+  if (int e = fused_scratch_address(&scratch)) return e;
+  // The arrival count must start at zero; a launch that gave up part-way may
+  // have left it otherwise.  The other words need no clearing.
+  if (cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream))
+    return nvfp4::cuda_status(e);
+  return rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count, (cudaStream_t)stream,
+                    k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n, nullptr, 0,
+                    1, 0, amax_out, scratch);
 }
 
 NVFP4_API int nvfp4_quantize_rht_fused_sharded_exchange(

@@ -38,7 +38,9 @@ enum nvfp4_status {
   NVFP4_ERR_MISALIGNED = 3,       /* a pointer misses the alignment TMA / vector I/O needs */
   NVFP4_ERR_CUDA = 4,             /* a CUDA runtime call failed (see nvfp4_last_cuda_error) */
   NVFP4_ERR_UNSUPPORTED_DEVICE = 5, /* not a compute capability 10.0 device */
-  NVFP4_ERR_DEVICE_TIMEOUT = 6    /* a kernel's bounded wait gave up (nvfp4_device_error) */
+  NVFP4_ERR_DEVICE_TIMEOUT = 6,   /* a kernel's bounded wait gave up (nvfp4_device_error) */
+  NVFP4_ERR_SCRATCH_CAPACITY = 7  /* more blocks than nvfp4_quantize_rht_fused_noalloc's
+                                     built-in scratch holds (1024) */
 };
 
 /* Human-readable text for a status code. */
@@ -121,6 +123,29 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
                                        uint32_t sm_count, nvfp4_stream_t stream, int k_tile_size,
                                        int stochastic_rounding, int use_fast_math,
                                        void* workspace);
+/* nvfp4_quantize_rht_fused for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some hosts own every byte of device
+ * memory through their own pool and do not let a library call cudaMalloc
+ * (it can synchronize the device and bypasses the pool), so they cannot
+ * provide nvfp4_quantize_rht_fused's workspace.  This entry point takes the
+ * same inputs and outputs but keeps the grid-barrier scratch in a 4112-byte
+ * array built into the library: every GPU that loads the library holds it
+ * until the process exits, and no call allocates anything.
+ *   - Limit: a launch may use at most 1024 blocks (one per SM is used);
+ *     beyond that it returns NVFP4_ERR_SCRATCH_CAPACITY.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array: calls that may overlap on the GPU (other
+ *     streams, other host threads) race and must be serialized by the caller.
+ *     Each call clears the arrival counter it needs at zero (a 4-byte
+ *     cudaMemsetAsync on `stream`); the array otherwise keeps the last call's
+ *     contents. */
+NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, const void* B,
+                                               void* C, void* SFC, float* amax_out,
+                                               const size_t* rng_state, uint32_t sm_count,
+                                               nvfp4_stream_t stream, int k_tile_size,
+                                               int stochastic_rounding, int use_fast_math);
+
 /* The same for one rank's column shard; the kernel also combines the ranks'
  * amax over peer memory (see nvfp4_exchange_create). */
 NVFP4_API int nvfp4_quantize_rht_fused_sharded_exchange(

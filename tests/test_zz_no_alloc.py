@@ -1,0 +1,61 @@
+"""The fused amax + cast entry point that allocates nothing.
+
+Callers that cannot allocate device memory -- hosts that hand out every byte
+through their own pool and do not allow a library to call cudaMalloc -- use
+nvfp4_quantize_rht_fused_noalloc, whose grid-barrier scratch is built into the
+library.  This test calls it through the C ABI twice in a row (the built-in
+scratch is reused) and checks every output against the existing entry point
+that takes a caller-provided workspace, bit for bit (the same tolerance as the
+other parity tests of this kernel).  It is collected last so that a run that
+stops at the first failure has run every other test first; it also passes
+alone in a fresh process."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_noalloc_matches_workspace_entry_twice():
+    from fp4_sm120a_b200 import _native, ops
+    from tests.gpu_helpers import activations, dev, h16
+    lib = _native.load()
+    rng = np.random.default_rng(99)
+    for m, n, sr, fm in [(1024, 2048, 1, 0), (384, 320, 0, 0), (5120, 8192, 1, 0)]:
+        A = dev(activations(rng, m * n))
+        B = dev(h16())
+        rs = torch.tensor([7, 3], dtype=torch.int64, device="cuda")
+        C0 = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
+        S0 = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
+        am0 = torch.empty(1, device="cuda")
+        ops.quantize_rht_fused(m, n, A, B, C0, S0, am0, rs, ops.fused_workspace(), 0, None,
+                               2048, stochastic_rounding=bool(sr), use_fast_math=bool(fm))
+        stream = torch.cuda.current_stream().cuda_stream
+        for _ in range(2):
+            C = torch.full_like(C0, 0xAA)
+            S = torch.full_like(S0, 0xAA)
+            am = torch.full((1,), -1.0, device="cuda")
+            rc = lib.nvfp4_quantize_rht_fused_noalloc(
+                m, n, A.data_ptr(), B.data_ptr(), C.data_ptr(), S.data_ptr(), am.data_ptr(),
+                rs.data_ptr(), 0, ctypes.c_void_p(stream), 2048, sr, fm)
+            assert rc == 0, lib.nvfp4_status_string(rc)
+            torch.cuda.synchronize()
+            assert ops.device_error() == 0
+            assert torch.equal(am.view(torch.int32), am0.view(torch.int32))
+            assert torch.equal(S, S0)
+            assert torch.equal(C, C0)
+
+
+def test_noalloc_rejects_more_blocks_than_its_scratch_holds():
+    from fp4_sm120a_b200 import _native
+    lib = _native.load()
+    if torch.cuda.get_device_properties(0).multi_processor_count <= 1024:
+        # sm_count above the device's SM count is capped to it, so on a B200
+        # (148 SMs) the limit cannot be exceeded; check the documented code.
+        assert b"scratch" in lib.nvfp4_status_string(7)
+    else:
+        rc = lib.nvfp4_quantize_rht_fused_noalloc(128, 64, 16, 16, 16, 16, None, None, 2048,
+                                                  None, 2048, 0, 0)
+        assert rc == 7
