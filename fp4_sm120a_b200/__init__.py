@@ -1,6 +1,7 @@
 """B200-native (sm_100a) NVFP4 quantization: the RHT GEMM + NVFP4 cast
-(rht_gemm_ntt_w_sfc) and the four FP4 stochastic-rounding conversions of
-Harry-Chen/fp4_sm120a, behind a C ABI (include/nvfp4_b200.h)."""
+(rht_gemm_ntt_w_sfc), the four FP4 stochastic-rounding conversions and the
+scaled FP8 conversions of Harry-Chen/fp4_sm120a, behind a C ABI
+(include/nvfp4_b200.h)."""
 from ._native import NVFP4Error, library_path, load  # noqa: F401
 from .ops import (  # noqa: F401
     amax_bf16,
@@ -10,6 +11,8 @@ from .ops import (  # noqa: F401
     mul_cvt_bf16_to_fp4_4x_sr,
     mul_cvt_bf16_to_fp4_8x_sr,
     mul_cvt_fp32_to_fp4_4x_sr,
+    mul_cvt_fp8_2x,
+    mul_cvt_fp8_4x,
     quantize_rht,
     quantize_rht_fused,
     quantize_rht_fused_sharded_exchange,

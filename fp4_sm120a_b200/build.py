@@ -18,7 +18,7 @@ LIB = PKG / "libnvfp4_b200.so"
 OBJDIR = PKG / "_build"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["rht_gemm_sm100.cu", "sr_kernels.cu"]
+SOURCES = ["rht_gemm_sm100.cu", "sr_kernels.cu", "fp8_kernels.cu", "fp8_kernels_loose.cu"]
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",

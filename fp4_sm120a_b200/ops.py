@@ -180,6 +180,37 @@ def amax_bf16(x: Ptr, n: int, out: Ptr, stream=None) -> None:
     call("nvfp4_amax_bf16", _ptr(x), n, _ptr(out), _stream(stream))
 
 
+DTYPE_CODES = {"f32": 0, "bf16": 1, "f16": 2}
+FP8_FORMATS = {"e4m3": 0, "e5m2": 1}
+
+
+def _dtype_code(dtype) -> int:
+    if isinstance(dtype, str):
+        return DTYPE_CODES[dtype]
+    return {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dtype]
+
+
+def mul_cvt_fp8_2x(inp: Ptr, in_dtype, scale: Ptr, scale_stride: int, out: Ptr, fmt: str,
+                   ngroups: int, stream=None) -> None:
+    """mul_cvt_2x over `ngroups` element pairs (te_ref ptx.cuh:923-1062)."""
+    call("nvfp4_mul_cvt_fp8_2x", _ptr(inp), _dtype_code(in_dtype), _ptr(scale), scale_stride,
+         _ptr(out), FP8_FORMATS[fmt], ngroups, _stream(stream))
+
+
+def mul_cvt_fp8_4x(inp: Ptr, in_dtype, scale: Ptr, scale_width: int, scale_stride: int,
+                   out: Ptr, fmt: str, ngroups: int, loose: bool = False, stream=None) -> None:
+    """mul_cvt_4x over `ngroups` groups of 4 (ptx.cuh:1172-1693); `loose` is the
+    _LOOSE_PRECISION build (floatx2 scale only)."""
+    if loose:
+        if scale_width != 2:
+            raise ValueError("the _LOOSE_PRECISION form takes a floatx2 scale")
+        call("nvfp4_mul_cvt_fp8_4x_loose", _ptr(inp), _dtype_code(in_dtype), _ptr(scale),
+             scale_stride, _ptr(out), FP8_FORMATS[fmt], ngroups, _stream(stream))
+    else:
+        call("nvfp4_mul_cvt_fp8_4x", _ptr(inp), _dtype_code(in_dtype), _ptr(scale), scale_width,
+             scale_stride, _ptr(out), FP8_FORMATS[fmt], ngroups, _stream(stream))
+
+
 def device_error(clear: bool = True) -> int:
     import ctypes
     code = ctypes.c_uint32(0)

@@ -4,6 +4,7 @@
     python -m fp4_sm120a_b200.profile_case amax --m 14336 --n 8192
     python -m fp4_sm120a_b200.profile_case sr   --groups 67108864
     python -m fp4_sm120a_b200.profile_case rowwise --m 16384 --n 8192
+    python -m fp4_sm120a_b200.profile_case fp8  --groups 67108864
     ... --time 20      # time 20 launches instead (L2 flushed before each)
 
 Each case runs `--launches` launches of one kernel on seeded inputs and exits
@@ -72,6 +73,13 @@ def _case(a, g):
         S = torch.empty(rows * cols // 16, dtype=torch.uint8, device="cuda")
         return ((lambda: ops.quantize_rowwise_bf16_sr(rows, cols, X, am, rb, C, S)),
                 rows * cols * 3.5625, rows * cols)
+    if a.kernel == "fp8":
+        # mul_cvt_4x, bf16 in, E4M3 out, one floatx2 scale: 8 + 4 B per group
+        x = torch.randn(4 * a.groups, device="cuda", generator=g).to(torch.bfloat16)
+        s = torch.tensor([0.5, 2.0], device="cuda")
+        out = torch.empty(4 * a.groups, dtype=torch.uint8, device="cuda")
+        return ((lambda: ops.mul_cvt_fp8_4x(x, "bf16", s, 2, 0, out, "e4m3", a.groups)),
+                a.groups * 12, 4 * a.groups)
     x = torch.randn(4 * a.groups, device="cuda", generator=g) * 3
     rb = torch.randint(-2**31, 2**31 - 1, (a.groups,), device="cuda", dtype=torch.int32,
                        generator=g)
@@ -82,7 +90,7 @@ def _case(a, g):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["rht", "amax", "sr", "rowwise", "fused", "twostep"])
+    ap.add_argument("kernel", choices=["rht", "amax", "sr", "rowwise", "fused", "twostep", "fp8"])
     ap.add_argument("--m", type=int, default=14336)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--sr", type=int, default=1)
@@ -108,7 +116,7 @@ def main(argv=None) -> int:
         ts.sort()
         ms = ts[len(ts) // 2]
         print(json.dumps({"kernel": a.kernel, "m": a.m, "n": a.n, "sr": a.sr, "fm": a.fm,
-                          "groups": a.groups if a.kernel == "sr" else None, "ms": ms,
+                          "groups": a.groups if a.kernel in ("sr", "fp8") else None, "ms": ms,
                           "gbs": nbytes / ms / 1e6, "elem_per_s": elems / ms * 1e3}))
     else:
         for _ in range(a.launches):

@@ -220,6 +220,34 @@ NVFP4_API int nvfp4_quantize_rowwise_bf16_sr(int rows, int cols, const void* X,
 NVFP4_API int nvfp4_amax_bf16(const void* x, size_t n, float* out, nvfp4_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* Scaled FP8 conversions (include/nvfp4_fp8.cuh) over batches of groups    */
+/* ---------------------------------------------------------------------- */
+
+/* Input element types and FP8 formats of the FP8 conversions. */
+enum { NVFP4_DTYPE_F32 = 0, NVFP4_DTYPE_BF16 = 1, NVFP4_DTYPE_F16 = 2 };
+enum { NVFP4_FP8_E4M3 = 0, NVFP4_FP8_E5M2 = 1 };
+
+/* mul_cvt_2x (te_ref ptx.cuh:923-1062): group g converts input elements
+ * 2g, 2g+1 (in_dtype) times the floatx2 at scale + g * scale_stride (stride
+ * in floats; 0 = one scale for every group) into FP8 bytes 2g, 2g+1 of out.
+ * Round to nearest even, saturating to the largest finite value. */
+NVFP4_API int nvfp4_mul_cvt_fp8_2x(const void* in, int in_dtype, const float* scale,
+                                   size_t scale_stride, void* out, int fp8_format,
+                                   size_t ngroups, nvfp4_stream_t stream);
+/* mul_cvt_4x (ptx.cuh:1172-1693): group g converts elements 4g .. 4g+3 into
+ * bytes 4g .. 4g+3.  scale_width 2: a floatx2 (elements 0, 2 take .x and 1, 3
+ * take .y); scale_width 4: a floatx4, one component per element. */
+NVFP4_API int nvfp4_mul_cvt_fp8_4x(const void* in, int in_dtype, const float* scale,
+                                   int scale_width, size_t scale_stride, void* out,
+                                   int fp8_format, size_t ngroups, nvfp4_stream_t stream);
+/* mul_cvt_4x with a floatx2 scale as built with the reference's
+ * _LOOSE_PRECISION macro: cvt.rs.satfinite.{e4m3,e5m2}x4.f32 with the constant
+ * random word 0x80008000 instead of round-to-nearest. */
+NVFP4_API int nvfp4_mul_cvt_fp8_4x_loose(const void* in, int in_dtype, const float* scale,
+                                         size_t scale_stride, void* out, int fp8_format,
+                                         size_t ngroups, nvfp4_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Diagnostics                                                             */
 /* ---------------------------------------------------------------------- */
 

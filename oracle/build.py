@@ -8,6 +8,8 @@ Two outputs:
                      rht_gemm/test_correctness.cu (nvcc host code)
       libref_gpu.so  TE's SM100 rht_gemm_ntt_w_sfc (rht_gemm/test_compare_ref.cu)
                      and TE's native cvt.rs functions (ptx.cuh), sm_100a.
+      libref_fp8.so  TE's scaled FP8 conversions mul_cvt_2x / mul_cvt_4x
+                     (ptx.cuh:923-1693), default and _LOOSE_PRECISION builds.
 
 The reference tree is located by $NVFP4_REFERENCE_ROOT (default: the mount
 point used by this build's containers).  On the GPU box the tree is absent and
@@ -111,6 +113,24 @@ def build_ref(force: bool = False) -> dict[str, Path]:
                   f"-I{rht_dir}", f"-I{rht_dir / 'te_ref' / 'stubs'}",
                   str(SHIMS / "ref_gpu_teref.cu"), "-o", str(gpu)])
         outs["gpu"] = gpu
+
+        # The reference's scaled FP8 conversions (ptx.cuh:923-1693), default
+        # and _LOOSE_PRECISION builds linked into one library.
+        fp8 = REF_OUT / "libref_fp8.so"
+        stubs = rht_dir / "te_ref" / "stubs"
+        fp8_deps = [SHIMS / "ref_gpu_fp8.cu", stubs / "common" / "util" / "ptx.cuh"]
+        if force or _stale(fp8, fp8_deps):
+            objs = []
+            for tag, defs in (("rn", []), ("loose", ["-D_LOOSE_PRECISION", "-DREF_FP8_LOOSE"])):
+                o = REF_OUT / f"ref_gpu_fp8_{tag}.o"
+                _run([NVCC, *ARCH, "-O3", "-std=c++20", "--expt-relaxed-constexpr",
+                      "-Xcompiler", "-fPIC", *defs, f"-I{cut / 'include'}", f"-I{stubs}",
+                      "-c", str(SHIMS / "ref_gpu_fp8.cu"), "-o", str(o)])
+                objs.append(o)
+            _run([NVCC, *ARCH, "-shared", *map(str, objs), "-o", str(fp8)])
+            for o in objs:
+                o.unlink()
+        outs["fp8"] = fp8
     return outs
 
 

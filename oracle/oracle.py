@@ -18,10 +18,8 @@ _LIB = None
 def lib() -> ctypes.CDLL:
     global _LIB
     if _LIB is None:
-        path = _HERE / "build" / "liboracle.so"
-        if not path.exists():
-            from . import build as _b
-            _b.build_oracle()
+        from . import build as _b
+        path = _b.build_oracle()     # no-op unless the C source is newer
         L = ctypes.CDLL(str(path))
         sig = {
             "orc_bf16_to_f32": ([ctypes.c_uint16], c_float),
@@ -45,6 +43,12 @@ def lib() -> ctypes.CDLL:
                                                c_size_t], None),
             "orc_mul_cvt_bf16_to_fp4_8x_sr": ([c_void_p, c_float, c_int, c_void_p, c_void_p,
                                                c_size_t], None),
+            "orc_f16_to_f32": ([ctypes.c_uint16], c_float),
+            "orc_f32_to_e5m2": ([c_float], c_uint8),
+            "orc_e5m2_to_f32": ([c_uint8], c_float),
+            "orc_set_e5m2_nan_code": ([c_uint8], None),
+            "orc_mul_cvt_fp8": ([c_void_p, c_int, c_void_p, c_size_t, c_int, c_int, c_int,
+                                 c_void_p, c_size_t], None),
             "orc_global_encode_scale": ([c_float], c_float),
             "orc_amax_bf16": ([c_void_p, c_size_t], c_float),
             "orc_rht_gemm_ntt_w_sfc": ([c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -116,6 +120,31 @@ def e2m1_sr_polyfill(x: float, rand_byte: int) -> int:
 
 def cvt_x4_polyfill(x4, word: int) -> int:
     return int(lib().orc_cvt_x4_polyfill(*(float(v) for v in x4), word))
+
+
+def e5m2(x: float) -> int:
+    return int(lib().orc_f32_to_e5m2(float(x)))
+
+
+def e5m2_decode(b: int) -> float:
+    return float(lib().orc_e5m2_to_f32(b))
+
+
+_DT = {"f32": (0, np.float32), "bf16": (1, np.uint16), "f16": (2, np.uint16)}
+
+
+def mul_cvt_fp8(x: np.ndarray, in_dtype: str, scale: np.ndarray, scale_stride: int, width: int,
+                scale_width: int, fmt: str) -> np.ndarray:
+    """mul_cvt_2x / mul_cvt_4x (te_ref ptx.cuh:923-1693) over a batch; x holds
+    f32 values or bf16 / f16 bit patterns (uint16), width * ngroups of them."""
+    code, dt = _DT[in_dtype]
+    x = np.ascontiguousarray(x, dt)
+    scale = np.ascontiguousarray(scale, np.float32)
+    ngroups = x.size // width
+    out = np.zeros(ngroups * width, np.uint8)
+    lib().orc_mul_cvt_fp8(_p(x), code, _p(scale), scale_stride, width, scale_width,
+                          {"e4m3": 0, "e5m2": 1}[fmt], _p(out), ngroups)
+    return out
 
 
 def e2m1_decode(nib) -> np.ndarray:

@@ -64,3 +64,28 @@ def gpu() -> ctypes.CDLL:
             getattr(L, f).restype = c_int
         _gpu = L
     return _gpu
+
+
+_fp8 = None
+
+
+def fp8_available() -> bool:
+    return (REF_DIR / "libref_fp8.so").exists()
+
+
+def fp8() -> ctypes.CDLL:
+    """The reference's own mul_cvt_2x / mul_cvt_4x (te_ref ptx.cuh:923-1693),
+    default and _LOOSE_PRECISION builds, one group per thread."""
+    global _fp8
+    if _fp8 is None:
+        L = ctypes.CDLL(str(REF_DIR / "libref_fp8.so"))
+        L.teref_mul_cvt_fp8_2x.argtypes = [c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int,
+                                           c_size_t, c_void_p]
+        L.teref_mul_cvt_fp8_4x.argtypes = [c_void_p, c_int, c_void_p, c_int, c_size_t, c_void_p,
+                                           c_int, c_size_t, c_void_p]
+        L.teref_mul_cvt_fp8_4x_loose.argtypes = [c_void_p, c_int, c_void_p, c_size_t, c_void_p,
+                                                 c_int, c_size_t, c_void_p]
+        for f in ("teref_mul_cvt_fp8_2x", "teref_mul_cvt_fp8_4x", "teref_mul_cvt_fp8_4x_loose"):
+            getattr(L, f).restype = c_int
+        _fp8 = L
+    return _fp8
