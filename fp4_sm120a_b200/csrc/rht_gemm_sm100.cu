@@ -298,6 +298,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmC, const Params p) {
   extern __shared__ uint8_t smem_raw[];
+  // Launched as a programmatic dependent of the previous kernel in the
+  // stream: the block is resident before that kernel has finished, and
+  // waits here until it has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -772,7 +776,20 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
     attr_set[dev] = true;
   }
   if constexpr (!FUSED) {
-    rht_nvfp4_kernel<SR, FM, FUSED><<<grid, kThreads, kSmemBytes, stream>>>(ta, tc, p);
+    // A programmatic dependent of the previous kernel in the stream: its
+    // launch and prologue overlap that kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, p))
+      return cuda_status(e);
   } else {
     // The fused kernel's blocks meet at a grid barrier: a cooperative launch
     // guarantees they are all resident (one per SM).

@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(256) k_quantize_rowwise_8x_sr(
 __global__ void __launch_bounds__(512) k_amax_bf16(const uint4* __restrict__ x, size_t nvec,
                                                    const uint16_t* __restrict__ tail, int ntail,
                                                    uint32_t* __restrict__ out_bits) {
+  // The next kernel (the cast) may launch now; it waits for this one to
+  // complete before it reads the amax.
+  asm volatile("griddepcontrol.launch_dependents;");
   uint32_t m2 = 0;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
