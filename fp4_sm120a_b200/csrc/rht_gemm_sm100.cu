@@ -8,18 +8,24 @@
 // round-to-nearest.  Results are bit-identical to TE's SM100 kernel
 // (rht_gemm/te_ref/hadamard_transform_cast_fusion_core.inc:92-506).
 //
-// Design (persistent, warp-specialised, one CTA per SM):
+// Design (warp-specialised, two CTAs per SM, each with its own pipeline, so
+// that the two epilogues do not advance in lockstep).  With every SM in use
+// the grid has one CTA per work unit and each running CTA takes the units of
+// CTAs that have not started yet through cluster launch control
+// (clusterlaunchcontrol.try_cancel), which balances the SMs and the two CTAs
+// of an SM; otherwise (fewer SMs requested, or the fused kernel's cooperative
+// launch) a persistent grid walks the units round-robin.
 //   work unit   128 rows x 256 columns of A (one output tile)
 //   warp 0      TMA producer: 128 x 64 bf16 sub-tiles (two 64 x 64 boxes,
-//               128-byte swizzle) into an 8-stage shared-memory ring
+//               128-byte swizzle) into a 4-stage shared-memory ring
 //   warp 1      tcgen05.mma issuer: per sub-tile four M128 N16 K16 bf16 MMAs
-//               (one per 16-column group) into a 4-stage TMEM ring of
-//               128-column fp32 accumulators; owns the TMEM allocation
-//   warps 2-17  epilogue: tcgen05.ld of a 32-column slice of its 32 TMEM lanes,
-//               bf16 round trip, amax, E4M3 scale, reciprocal, Philox, cvt.rs /
-//               cvt.rn; FP4 bytes staged in a swizzled 128 x 128 B tile that one
-//               TMA store writes out; scale bytes staged and copied out in
-//               16-byte rows.
+//               (one per 16-column group) into a 2-stage TMEM ring of
+//               128-column fp32 accumulators; owns the CTA's 256 TMEM columns
+//   warps 2-9   epilogue: tcgen05.ld of two 32-column slices of its 32 TMEM
+//               lanes per stage, bf16 round trip, amax, E4M3 scale,
+//               reciprocal, Philox, cvt.rs / cvt.rn; FP4 bytes staged in a
+//               swizzled 128 x 128 B tile that one TMA store writes out; scale
+//               bytes staged and copied out in 16-byte rows.
 // Every wait is bounded (1 s); a kernel that gives up records an error word
 // and unwinds (drains its TMA loads and MMAs, frees TMEM) instead of hanging.
 #include <cstdint>
@@ -47,9 +53,10 @@ constexpr int kBM = 128;          // rows per tile = TMEM lanes
 constexpr int kSubN = 64;         // columns per TMA sub-tile
 constexpr int kUnitN = 256;       // columns per work unit / output tile
 constexpr int kAccN = 128;        // fp32 columns per TMEM accumulator stage
-constexpr int kStages = 8;        // shared-memory ring depth
-constexpr int kAccStages = 4;     // 4 x 128 = all 512 TMEM columns
-constexpr int kEpiWarps = 16;
+constexpr int kStages = 4;        // shared-memory ring depth
+constexpr int kAccStages = 2;     // 2 x 128 = half the TMEM columns (two CTAs per SM)
+constexpr uint32_t kTmemCols = kAccStages * 128;
+constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kStageBytes = kBM * kSubN * 2;        // 16 KiB
@@ -62,8 +69,10 @@ constexpr uint32_t kOffA = 0;
 constexpr uint32_t kOffC = kOffA + kStages * kStageBytes;
 constexpr uint32_t kOffSfc = kOffC + 2 * kCTileBytes;
 constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
-constexpr uint32_t kOffBar = kOffB + 512;
-constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1;
+constexpr int kClcSlots = 4;      // cluster-launch-control response ring
+constexpr uint32_t kOffClc = kOffB + 512;                 // 16 B per response
+constexpr uint32_t kOffBar = kOffClc + 16 * kClcSlots;
+constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots;
 constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
 constexpr uint32_t kOffMisc = kOffTab + 256 * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
@@ -119,6 +128,10 @@ struct Params {
   // [0] arrival count, [1] generation, [2] amax bits, [3] unused,
   // [4 + b] amax bits of block b.  Zeroed once before first use.
   uint32_t* ws;
+  // 1: the grid has one CTA per work unit and running CTAs take the units of
+  // CTAs not yet started through cluster launch control (dynamic balance);
+  // 0: a persistent grid walks the units round-robin.
+  int dynamic;
 };
 
 constexpr int kMaxFusedCtas = 1024;
@@ -182,6 +195,11 @@ struct UnitIter {
   __device__ __forceinline__ void set(const Params& p) {
     un = (int)p.div_tiles_m.div((uint32_t)u);
     tm = u - un * p.tiles_m;
+  }
+  // Continue with unit u (dynamic schedule); u < 0 ends the walk.
+  __device__ __forceinline__ void jump(const Params& p, int nu) {
+    u = nu < 0 ? p.units : nu;
+    if (u < p.units) set(p);
   }
   __device__ __forceinline__ bool valid(const Params& p) const {
     return rev ? (u >= (int)blockIdx.x && u < p.units) : (u < p.units);
@@ -284,6 +302,30 @@ __device__ __forceinline__ void philox_pair(uint32_t x, uint32_t y, uint32_t z, 
   rb = make_uint4(b0, b1, b2, b3);
 }
 
+// Cluster launch control (one-CTA clusters): ask to cancel a CTA of this grid
+// that has not started yet; the 16-byte response lands in shared memory and
+// completes `bar` (transaction count 16).
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 "
+      "[%0], [%1];" ::"r"(resp), "r"(bar)
+      : "memory");
+}
+// The first CTA index a response names, or -1 if no CTA was cancelled.
+__device__ __forceinline__ int clc_decode(uint32_t resp) {
+  uint32_t x = 0, ok = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %1, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid.v4.b32.b128 {%0, _, _, _}, r;\n\t}"
+      : "+r"(x), "=r"(ok)
+      : "r"(resp)
+      : "memory");
+  return ok ? (int)x : -1;
+}
+
 // Warp-uniform bounded wait: every lane polls the barrier (no divergent
 // branch around the wait) and the warp agrees on the verdict with a vote.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
@@ -294,7 +336,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
 }
 
 template <bool SR, bool FM, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmC, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -319,6 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto empty1_bar = [&](uint32_t s) {
     return bar0 + 8 * (3 * kStages + 2 * kAccStages + 1 + s);
   };
+  auto clcf_bar = [&](uint32_t s) { return bar0 + 8 * (4 * kStages + 2 * kAccStages + 1 + s); };
+  auto clce_bar = [&](uint32_t s) {
+    return bar0 + 8 * (4 * kStages + 2 * kAccStages + 1 + kClcSlots + s);
+  };
+  auto clc_resp = [&](uint32_t s) { return sbase + kOffClc + 16 * s; };
+  // Unit number j >= 1 of this CTA under the dynamic schedule: the response of
+  // request j (slot (j - 1) % kClcSlots).  Every role reads every response
+  // once; -1 ends the walk (no CTA left to cancel, or a wait gave up).
+  auto clc_slot = [](uint32_t j) { return (j - 1) % (uint32_t)kClcSlots; };
+  auto clc_parity = [](uint32_t j) { return ((j - 1) / (uint32_t)kClcSlots) & 1u; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
 
@@ -335,6 +387,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (uint32_t st = 0; st < kStages; ++st) {
       mbar_init(full1_bar(st), 1);
       mbar_init(empty1_bar(st), kEpiThreads);
+    }
+    for (uint32_t sl = 0; sl < (uint32_t)kClcSlots; ++sl) {
+      mbar_init(clcf_bar(sl), 1);
+      mbar_init(clce_bar(sl), 2 + kEpiWarps);   // producer, MMA, one per epilogue warp
     }
     *abort_flag = 0u;
     fence_barrier_init();
@@ -355,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sb[off >> 1] = p.B[idx];
     }
     fence_proxy_async_smem();
-    tmem_alloc(smem_addr(tmem_holder), 512);
+    tmem_alloc(smem_addr(tmem_holder), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -404,7 +460,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       UnitIter it;
-      for (it.init(p, FUSED); it.valid(p) && ok; it.next(p)) {
+      uint32_t k = 0;               // index of the current unit
+      bool pending = false;         // a cancel request whose response is unread
+      for (it.init(p, FUSED); it.valid(p) && ok;) {
+        if (p.dynamic) {
+          // request the unit after this one while this one streams in
+          const uint32_t j = k + 1, sl = clc_slot(j);
+          if (!mbar_wait_bounded(clce_bar(sl), clc_parity(j) ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutProducer, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(clcf_bar(sl), 16);
+          clc_try_cancel(clc_resp(sl), clcf_bar(sl));
+          pending = true;
+        }
         const Unit t = unit_at(p, it);
         for (int s = 0; s < t.nsub; ++s) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kWaitLimitNs,
@@ -420,6 +490,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++issued;
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
+        if (!ok) break;
+        ++k;
+        if (p.dynamic) {
+          const uint32_t sl = clc_slot(k);
+          int nu = -1;
+          if (mbar_wait_bounded(clcf_bar(sl), clc_parity(k), abort_flag, kWaitLimitNs,
+                                kErrTimeoutProducer, &g_device_error_word)) {
+            nu = clc_decode(clc_resp(sl));
+            fence_proxy_async_smem();
+            mbar_arrive(clce_bar(sl));
+            pending = false;
+          } else {
+            ok = false;
+          }
+          it.jump(p, nu);
+        } else {
+          it.next(p);
+        }
+      }
+      if (pending) {
+        // A response still on its way lands before the CTA exits.
+        volatile uint32_t never = 0u;
+        mbar_wait_bounded(clcf_bar(clc_slot(k + 1)), clc_parity(k + 1), &never, kWaitLimitNs,
+                          kErrTimeoutDrain, &g_device_error_word);
       }
       if (!ok) {
         // Let the loads already in flight land before the CTA exits.
@@ -441,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0, acc = 0, accph = 0;
       bool ok = true;
       UnitIter it;
-      for (it.init(p, FUSED); it.valid(p) && ok; it.next(p)) {
+      uint32_t k = 0;
+      for (it.init(p, FUSED); it.valid(p) && ok;) {
         const Unit t = unit_at(p, it);
         for (int a = 0; a < t.nacc && ok; ++a) {
           if (!mbar_wait_bounded(acce_bar(acc), accph ^ 1u, abort_flag, kWaitLimitNs,
@@ -474,6 +569,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(accf_bar(acc));
           if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
         }
+        if (!ok) break;
+        ++k;
+        if (p.dynamic) {
+          const uint32_t sl = clc_slot(k);
+          int nu = -1;
+          if (mbar_wait_bounded(clcf_bar(sl), clc_parity(k), abort_flag, kWaitLimitNs,
+                                kErrTimeoutMma, &g_device_error_word)) {
+            nu = clc_decode(clc_resp(sl));
+            fence_proxy_async_smem();
+            mbar_arrive(clce_bar(sl));
+          } else {
+            ok = false;
+          }
+          it.jump(p, nu);
+        } else {
+          it.next(p);
+        }
       }
       // All issued MMAs complete before TMEM is released.
       tc_commit(drain_bar);
@@ -486,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ epilogue ----------------------------------
     const int ew = warp - 2;
     const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int slice = ew >> 2;        // 32-column slice of each accumulator stage
+    const int slice0 = ew >> 2;       // slices slice0 and slice0 + 2 of each stage
     const int r = q * 32 + lane;      // row within the 128-row tile
     const bool leader = (ew == 0 && lane == 0);
 
@@ -511,13 +623,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok1 = false;
             break;
           }
-          const uint4* src =
-              reinterpret_cast<const uint4*>(smem + kOffA + st1 * kStageBytes) + 2 * tid;
-          const uint4 x = src[0], y = src[1];
-          m2 = __vmaxu2(m2, x.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.y & 0x7FFF7FFFu);
-          m2 = __vmaxu2(m2, x.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.w & 0x7FFF7FFFu);
-          m2 = __vmaxu2(m2, y.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.y & 0x7FFF7FFFu);
-          m2 = __vmaxu2(m2, y.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.w & 0x7FFF7FFFu);
+#pragma unroll
+          for (int j = 0; j < (int)(kStageBytes / (32 * kEpiThreads)); ++j) {
+            const uint4* src = reinterpret_cast<const uint4*>(smem + kOffA + st1 * kStageBytes) +
+                               2 * (tid + j * kEpiThreads);
+            const uint4 x = src[0], y = src[1];
+            m2 = __vmaxu2(m2, x.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.y & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, x.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.w & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, y.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.y & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, y.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.w & 0x7FFF7FFFu);
+          }
           mbar_arrive(empty1_bar(st1));
           if (++st1 == kStages) { st1 = 0; ph1 ^= 1u; }
         }
@@ -589,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc = 0, accph = 0, ucount = 0;
     bool ok = true;
     UnitIter it;
-    for (it.init(p, FUSED); it.valid(p); it.next(p), ++ucount) {
+    for (it.init(p, FUSED); it.valid(p); ++ucount) {
       const Unit t = unit_at(p, it);
       const uint32_t buf = ucount & 1u;
       uint8_t* cst = smem + kOffC + buf * kCTileBytes;
@@ -600,48 +715,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t chunk0 = p.div_ktm.div(kb0);
       const uint32_t kt0 = kb0 - chunk0 * p.ktm;
       for (int a = 0; a < t.nacc && ok; ++a) {
-        const int blk = 2 * a + (slice >> 1);  // 64-column block within the unit
         // The random words depend only on coordinates, so they are generated
         // before waiting for the accumulator and overlap that wait.
-        uint4 rb0 = make_uint4(0, 0, 0, 0), rb1 = rb0;
-        if constexpr (SR) {
-          // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
-          // linear_tile = tile_m + tiles_m * chunk; generate4() number
-          // (column % 64) / 16 of that sequence.
-          uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
-          while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
-          const uint32_t L = (uint32_t)t.tm + (uint32_t)p.tiles_m * chunk;
-          const uint32_t seq = (uint32_t)r + kt * 256u + L * p.ktm * 256u;
-          // counter (offset_lo, offset_hi, seq, 0) advanced by 2 * (slice & 1)
-          uint32_t cx = olo + (uint32_t)(slice & 1) * 2u, cy = ohi, cz = seq, cw = 0;
-          if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
-          philox_pair(cx, cy, cz, cw, k0, k1, rb0, rb1);
+        uint4 rb[2][2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int slice = slice0 + 2 * j;
+          const int blk = 2 * a + (slice >> 1);
+          rb[j][0] = make_uint4(0, 0, 0, 0);
+          rb[j][1] = rb[j][0];
+          if constexpr (SR) {
+            // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
+            // linear_tile = tile_m + tiles_m * chunk; the counter
+            // (offset_lo, offset_hi, seq, 0) advanced by 2 * (slice & 1)
+            // gives generate4() numbers (column % 64) / 16 of that sequence.
+            uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
+            while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
+            const uint32_t L = (uint32_t)t.tm + (uint32_t)p.tiles_m * chunk;
+            const uint32_t seq = (uint32_t)r + kt * 256u + L * p.ktm * 256u;
+            uint32_t cx = olo + (uint32_t)(slice & 1) * 2u, cy = ohi, cz = seq, cw = 0;
+            if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
+            philox_pair(cx, cy, cz, cw, k0, k1, rb[j][0], rb[j][1]);
+          }
         }
         if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const bool valid = blk < t.nsub;
-        float v[32];
-        if (valid) {
-          tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
-          tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int slice = slice0 + 2 * j;
+          const int blk = 2 * a + (slice >> 1);
+          const bool valid = blk < t.nsub;
+          float v[32];
+          if (valid) {
+            tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
+            tc_wait_ld();
+          }
+          if (j == 1) {
+            tc_fence_before();
+            __syncwarp();
+            mbar_arrive(acce_bar(acc));
+          }
+          if (!valid) continue;
+          uint32_t w0, w1, w2, w3;
+          const uint32_t s0 = quant16<SR, FM>(v, enc_mult, acc_tab, rb[j][0], w0, w1);
+          const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, acc_tab, rb[j][1], w2, w3);
+          const uint32_t chunk16 = (uint32_t)(a * 4 + slice) ^ (uint32_t)(r & 7);
+          *reinterpret_cast<uint4*>(cst + r * 128 + chunk16 * 16) = make_uint4(w0, w1, w2, w3);
+          *reinterpret_cast<uint16_t*>(sst + r * 16 + a * 8 + slice * 2) =
+              (uint16_t)(s0 | (s1 << 8));
         }
-        tc_fence_before();
-        __syncwarp();
-        mbar_arrive(acce_bar(acc));
         if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
-        if (!valid) continue;
-
-        uint32_t w0, w1, w2, w3;
-        const uint32_t s0 = quant16<SR, FM>(v, enc_mult, acc_tab, rb0, w0, w1);
-        const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, acc_tab, rb1, w2, w3);
-        // swizzled (128-byte pattern) FP4 tile row r, 16-byte chunk a*4+slice
-        const uint32_t chunk16 = (uint32_t)(a * 4 + slice) ^ (uint32_t)(r & 7);
-        *reinterpret_cast<uint4*>(cst + r * 128 + chunk16 * 16) = make_uint4(w0, w1, w2, w3);
-        *reinterpret_cast<uint16_t*>(sst + r * 16 + a * 8 + slice * 2) =
-            (uint16_t)(s0 | (s1 << 8));
       }
       // One barrier per unit among the epilogue warps.  Before it, the leader
       // waits until the previous TMA store has read its staging buffer, which
@@ -652,6 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, kEpiThreads);
       if (!ok || *abort_flag) {
         ok = false;
+        if (p.dynamic) it.jump(p, -1);
+        else it.next(p);
         continue;
       }
       if (leader) {
@@ -672,6 +800,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int b = 0; b < nbytes; ++b) dst[b] = src[b];
         }
       }
+      if (p.dynamic) {
+        // every lane reads the response; lane 0 releases the slot for the warp
+        const uint32_t j = ucount + 1, sl = clc_slot(j);
+        int nu = -1;
+        if (ok && warp_wait(clcf_bar(sl), clc_parity(j), abort_flag, kErrTimeoutEpilogue)) {
+          nu = clc_decode(clc_resp(sl));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(clce_bar(sl));
+        }
+        it.jump(p, nu);
+      } else {
+        it.next(p);
+      }
     }
     if (leader) bulk_wait_all();
     __syncwarp();
@@ -681,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -773,6 +915,11 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemBytes))
       return cuda_status(e);
+    // The largest shared-memory carveout, so that two CTAs fit on every SM.
+    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM, FUSED>,
+                                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared))
+      return cuda_status(e);
     attr_set[dev] = true;
   }
   if constexpr (!FUSED) {
@@ -792,7 +939,17 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
       return cuda_status(e);
   } else {
     // The fused kernel's blocks meet at a grid barrier: a cooperative launch
-    // guarantees they are all resident (one per SM).
+    // guarantees they are all resident.  It admits as many blocks per SM as
+    // the occupancy calculator reports for this kernel (one on current
+    // drivers, which count the TMEM-allocating kernel as one per SM, although
+    // two run side by side when launched normally).
+    int per_sm = 0, sms = 0;
+    if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, rht_nvfp4_kernel<SR, FM, FUSED>, kThreads, kSmemBytes))
+      return cuda_status(e);
+    if (int e = device_sm_count(&sms)) return e;
+    if (per_sm < 1) return cuda_status(cudaErrorCooperativeLaunchTooLarge);
+    if (grid > per_sm * sms) grid = per_sm * sms;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -855,10 +1012,17 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.epoch = ex_epoch;
   p.amax_out = amax_out;
   p.ws = fused_ws;
+  p.dynamic = 0;
 
   int grid = sms;
   if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
+  grid *= 2;   // two CTAs per SM
   if (p.units < grid) grid = p.units;
+  if (!fused && grid == 2 * sms) {
+    // All SMs in use: one CTA per unit, balanced by cluster launch control.
+    p.dynamic = 1;
+    grid = p.units;
+  }
 
   if (fused) {
     if (grid > kMaxFusedCtas) grid = kMaxFusedCtas;
