@@ -72,7 +72,7 @@ constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
 constexpr int kClcSlots = 4;      // cluster-launch-control response ring
 constexpr uint32_t kOffClc = kOffB + 512;                 // 16 B per response
 constexpr uint32_t kOffBar = kOffClc + 16 * kClcSlots;
-constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots;
+constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots + 1;
 constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
 constexpr uint32_t kOffMisc = kOffTab + 256 * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
@@ -132,6 +132,8 @@ struct Params {
   // CTAs not yet started through cluster launch control (dynamic balance);
   // 0: a persistent grid walks the units round-robin.
   int dynamic;
+  // 1: B arrives by one TMA load (B 16-byte aligned); 0: warp 1 copies it.
+  int b_tma;
 };
 
 constexpr int kMaxFusedCtas = 1024;
@@ -302,6 +304,15 @@ __device__ __forceinline__ void philox_pair(uint32_t x, uint32_t y, uint32_t z, 
   rb = make_uint4(b0, b1, b2, b3);
 }
 
+// 4-D TMA tile load (the B matrix in its canonical no-swizzle layout).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %3, %3, %3}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(bar), "r"(0)
+      : "memory");
+}
+
 // Cluster launch control (one-CTA clusters): ask to cancel a CTA of this grid
 // that has not started yet; the 16-byte response lands in shared memory and
 // completes `bar` (transaction count 16).
@@ -338,7 +349,8 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
 template <bool SR, bool FM, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 2)
     rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmC, const Params p) {
+                     const __grid_constant__ CUtensorMap tmC,
+                     const __grid_constant__ CUtensorMap tmB, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   // Launched as a programmatic dependent of the previous kernel in the
   // stream: the block is resident before that kernel has finished, and
@@ -371,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // once; -1 ends the walk (no CTA left to cancel, or a wait gave up).
   auto clc_slot = [](uint32_t j) { return (j - 1) % (uint32_t)kClcSlots; };
   auto clc_parity = [](uint32_t j) { return ((j - 1) / (uint32_t)kClcSlots) & 1u; };
+  const uint32_t bfull_bar = bar0 + 8 * (kNumBars - 1);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
 
@@ -388,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(full1_bar(st), 1);
       mbar_init(empty1_bar(st), kEpiThreads);
     }
+    mbar_init(bfull_bar, 1);
     for (uint32_t sl = 0; sl < (uint32_t)kClcSlots; ++sl) {
       mbar_init(clcf_bar(sl), 1);
       mbar_init(clce_bar(sl), 2 + kEpiWarps);   // producer, MMA, one per epilogue warp
@@ -398,19 +412,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmC);
+    if (p.b_tma) prefetch_tmap(&tmB);
   }
   float* acc_tab = reinterpret_cast<float*>(smem + kOffTab);
   float* s_amax = reinterpret_cast<float*>(smem + kOffMisc + 8);
   if (warp == 1) {
-    // B into shared memory in the canonical no-swizzle MN-major layout:
-    // B(n = c, k) at (c % 8) * 2 + (k % 8) * 16 + (c / 8) * 128 + (k / 8) * 256.
-    uint16_t* sb = reinterpret_cast<uint16_t*>(smem + kOffB);
-    for (int idx = lane; idx < 256; idx += 32) {
-      const int k = idx >> 4, c = idx & 15;
-      const uint32_t off = (c & 7) * 2 + (k & 7) * 16 + (c >> 3) * 128 + (k >> 3) * 256;
-      sb[off >> 1] = p.B[idx];
+    if (!p.b_tma) {
+      // B into shared memory in the canonical no-swizzle MN-major layout:
+      // B(n = c, k) at (c % 8) * 2 + (k % 8) * 16 + (c / 8) * 128 + (k / 8) * 256.
+      uint16_t* sb = reinterpret_cast<uint16_t*>(smem + kOffB);
+      for (int idx = lane; idx < 256; idx += 32) {
+        const int k = idx >> 4, c = idx & 15;
+        const uint32_t off = (c & 7) * 2 + (k & 7) * 16 + (c >> 3) * 128 + (k >> 3) * 256;
+        sb[off >> 1] = p.B[idx];
+      }
+      fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
     tmem_alloc(smem_addr(tmem_holder), kTmemCols);
     tmem_relinquish();
   }
@@ -424,6 +441,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
+      if (p.b_tma) {
+        // B in the canonical no-swizzle MN-major layout, straight from the
+        // 4-D view (c % 8, k % 8, c / 8, k / 8) of the row-major 16 x 16 matrix.
+        mbar_arrive_expect_tx(bfull_bar, 512);
+        tma_load_4d(sbase + kOffB, &tmB, bfull_bar);
+      }
       if constexpr (FUSED) {
         // First pass: the same tiles, forward, for the epilogue's amax; its
         // own barriers (full1 / empty1) over the same ring stages.
@@ -517,6 +540,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (!ok) {
         // Let the loads already in flight land before the CTA exits.
+        volatile uint32_t never_b = 0u;
+        if (p.b_tma)
+          mbar_wait_bounded(bfull_bar, 0, &never_b, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
         uint32_t st = stage, ph = phase;
         const uint32_t n_pending = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
         volatile uint32_t never = 0u;
@@ -534,6 +561,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t bdesc = umma_smem_desc(sbase + kOffB, 256, 128, 0);
       uint32_t stage = 0, phase = 0, acc = 0, accph = 0;
       bool ok = true;
+      if (p.b_tma && !mbar_wait_bounded(bfull_bar, 0, abort_flag, kWaitLimitNs, kErrTimeoutMma,
+                                        &g_device_error_word))
+        ok = false;
       UnitIter it;
       uint32_t k = 0;
       for (it.init(p, FUSED); it.valid(p) && ok;) {
@@ -887,6 +917,17 @@ int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* o
     res = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estride,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (kind == 2) {
+    // B: the row-major 16 x 16 bf16 matrix seen as (c % 8, k % 8, c / 8, k / 8)
+    // with byte strides 2, 32, 16, 256; one 8 x 8 x 2 x 2 box lands in shared
+    // memory in the canonical no-swizzle MN-major layout of the MMA's B operand.
+    const cuuint64_t dims[4] = {8, 8, 2, 2};
+    const cuuint64_t strides[3] = {32, 16, 256};
+    const cuuint32_t box[4] = {8, 8, 2, 2};
+    const cuuint32_t es4[4] = {1, 1, 1, 1};
+    res = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, ptr, dims, strides, box, es4,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
     // C: bytes, dims {n/2, m}, box 128 x 128, 128-byte swizzle
     const cuuint64_t dims[2] = {d0, d1};
@@ -905,8 +946,8 @@ int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* o
 }
 
 template <bool SR, bool FM, bool FUSED>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p, int grid,
-                  cudaStream_t stream) {
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tb,
+                  const Params& p, int grid, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
@@ -935,7 +976,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, p))
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
       return cuda_status(e);
   } else {
     // The fused kernel's blocks meet at a grid barrier: a cooperative launch
@@ -960,7 +1001,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const Params& p,
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, p))
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
       return cuda_status(e);
   }
   return cuda_status(cudaGetLastError());
@@ -987,7 +1028,8 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   int sms = 0;
   if (int e = device_sm_count(&sms)) return e;
 
-  CUtensorMap ta, tc;
+  CUtensorMap ta, tc, tb;
+  std::memset(&tb, 0, sizeof(tb));
   if (int e = get_tensor_map(0, const_cast<void*>(A), (uint64_t)m, (uint64_t)n, &ta)) return e;
   if (int e = get_tensor_map(1, C, (uint64_t)(n / 2), (uint64_t)m, &tc)) return e;
 
@@ -1013,6 +1055,9 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.amax_out = amax_out;
   p.ws = fused_ws;
   p.dynamic = 0;
+  p.b_tma = (reinterpret_cast<uintptr_t>(B) % 16 == 0) ? 1 : 0;
+  // (a B whose view the driver will not encode takes the copy path instead)
+  if (p.b_tma && get_tensor_map(2, const_cast<void*>(B), 16, 16, &tb) != NVFP4_OK) p.b_tma = 0;
 
   int grid = sms;
   if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
@@ -1026,15 +1071,15 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
 
   if (fused) {
     if (grid > kMaxFusedCtas) grid = kMaxFusedCtas;
-    if (sr && fm) return launch_kernel<true, true, true>(ta, tc, p, grid, stream);
-    if (sr) return launch_kernel<true, false, true>(ta, tc, p, grid, stream);
-    if (fm) return launch_kernel<false, true, true>(ta, tc, p, grid, stream);
-    return launch_kernel<false, false, true>(ta, tc, p, grid, stream);
+    if (sr && fm) return launch_kernel<true, true, true>(ta, tc, tb, p, grid, stream);
+    if (sr) return launch_kernel<true, false, true>(ta, tc, tb, p, grid, stream);
+    if (fm) return launch_kernel<false, true, true>(ta, tc, tb, p, grid, stream);
+    return launch_kernel<false, false, true>(ta, tc, tb, p, grid, stream);
   }
-  if (sr && fm) return launch_kernel<true, true, false>(ta, tc, p, grid, stream);
-  if (sr) return launch_kernel<true, false, false>(ta, tc, p, grid, stream);
-  if (fm) return launch_kernel<false, true, false>(ta, tc, p, grid, stream);
-  return launch_kernel<false, false, false>(ta, tc, p, grid, stream);
+  if (sr && fm) return launch_kernel<true, true, false>(ta, tc, tb, p, grid, stream);
+  if (sr) return launch_kernel<true, false, false>(ta, tc, tb, p, grid, stream);
+  if (fm) return launch_kernel<false, true, false>(ta, tc, tb, p, grid, stream);
+  return launch_kernel<false, false, false>(ta, tc, tb, p, grid, stream);
 }
 
 }  // namespace rht
