@@ -141,7 +141,8 @@ constexpr int kFusedWsWords = 4 + kMaxFusedCtas;
 
 // The global amax of this launch.  With world > 1: block 0 publishes
 // {epoch, bits of this rank's amax} into slot `rank` of every rank's slot
-// array (system-scope release stores over NVLink), then every block polls
+// array (system-scope relaxed 64-bit stores over NVLink: the word carries its
+// whole payload, so no release fence is needed), then every block polls
 // its own rank's slots until all `world` of them carry this epoch and takes
 // the bitwise max (amax >= 0, so integer order is value order and NaN wins).
 // Slots alternate by epoch parity: a rank can be at most one launch ahead of
@@ -156,20 +157,20 @@ __device__ __forceinline__ float launch_amax(const Params& p, float local,
     const uint32_t bits = __float_as_uint(local);
     const unsigned long long val = ((unsigned long long)p.epoch << 32) | bits;
     for (int q = 0; q < p.world; ++q)
-      st_release_sys_u64(const_cast<unsigned long long*>(p.peers[q]) + par * p.world + p.rank, val);
+      st_relaxed_sys_u64(const_cast<unsigned long long*>(p.peers[q]) + par * p.world + p.rank, val);
   }
   const unsigned long long* mine = p.peers[p.rank] + par * p.world;
   uint32_t mx = 0;
   const uint64_t t0 = globaltimer_ns();
   for (int q = 0; q < p.world; ++q) {
-    unsigned long long v = ld_acquire_sys_u64(mine + q);
+    unsigned long long v = ld_relaxed_sys_u64(mine + q);
     while ((uint32_t)(v >> 32) != p.epoch) {
       if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1u;
         atomicCAS(&g_device_error_word, 0u, (uint32_t)kErrTimeoutExchange);
         return __uint_as_float(0x7FFFFFFFu);
       }
-      v = ld_acquire_sys_u64(mine + q);
+      v = ld_relaxed_sys_u64(mine + q);
     }
     mx = max(mx, (uint32_t)v);
   }
