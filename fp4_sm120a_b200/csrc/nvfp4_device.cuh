@@ -205,7 +205,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
-// System-scope release store / acquire load of 64 bits (peer-memory flags).
 // System-scope relaxed store / load of 64 bits: for a flag word that carries
 // all of its payload itself (no other data is published through it), so no
 // ordering fence is needed -- only single-copy atomicity and visibility.
@@ -215,14 +214,6 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
