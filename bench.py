@@ -59,8 +59,71 @@ def dist_env():
     return ws, rank, local
 
 
+class NvmlClockSampler:
+    """SM clock and throttle-reason sampling during the timed region, read
+    from NVML every ~0.5 ms in a thread (read-only queries), so that timed
+    regions of a few milliseconds still get samples."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+
+    def __init__(self, cuda_indices):
+        import threading
+        import pynvml
+        import torch
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.handles = []
+        for i in cuda_indices:
+            pr = torch.cuda.get_device_properties(i)
+            try:
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self.handles.append(pynvml.nvmlDeviceGetHandleByPciBusId(bus))
+            except Exception:
+                self.handles.append(pynvml.nvmlDeviceGetHandleByIndex(i))
+        self.samples, self.reasons = [], set()
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handles[0], pynvml.NVML_CLOCK_SM)
+        self.stop = threading.Event()
+        self.active = threading.Event()   # sample only while set (GPU busy windows)
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            if not self.active.wait(timeout=0.01):
+                continue
+            for h in self.handles:
+                try:
+                    self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for name, mask in self.REASONS.items():
+                        if bits & mask:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+            time.sleep(0.0005)
+
+    def __enter__(self):
+        self.thread.start()
+        return self
+
+    def window(self, on: bool):
+        (self.active.set if on else self.active.clear)()
+
+    def __exit__(self, *a):
+        self.active.clear()
+        self.stop.set()
+        self.thread.join(timeout=5)
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples), "source": "NVML"}
+
+
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling during the timed region (used when
+    NVML cannot be loaded)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -283,26 +346,36 @@ def bench_ours(args):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(gpu_list) if rank == 0 else None
+    sampler = None
+    if rank == 0:
+        try:
+            sampler = NvmlClockSampler(gpu_list)
+        except Exception:
+            sampler = ClockSampler(gpu_list)
     if sampler:
         sampler.__enter__()
+    window = getattr(sampler, "window", lambda on: None)
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    window(True)
     t0.record(stream)
     for i in range(args.steps):
         step()
     t1.record(stream)
     torch.cuda.synchronize()
+    window(False)
     # The cast's per-launch duration for the roofline: the same K steps again,
     # now with CUDA events around each cast.  They are kept out of the timed
     # steps above because an event recorded between the amax kernel and the
     # cast ends the cast's programmatic-dependent overlap with the amax.
     if ws > 1:
         dist.barrier()
+    window(True)
     for i in range(args.steps):
         step(evs[i])
     torch.cuda.synchronize()
+    window(False)
     if ws > 1:
         dist.barrier()
     if sampler:
