@@ -1318,6 +1318,11 @@ NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, cons
                                                const size_t* rng_state, uint32_t sm_count,
                                                nvfp4_stream_t stream, int k_tile_size,
                                                int stochastic_rounding, int use_fast_math) {
+  // Shape and pointer checks first, so that a refused call enqueues nothing.
+  if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
+  if (m == 0 || n == 0) return NVFP4_OK;
+  if (m % nvfp4::rht::kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
+  if (!A || !B || !C || !SFC) return NVFP4_ERR_INVALID_ARGUMENT;
   // The static scratch holds one partial amax per block, for at most
   // kMaxFusedCtas blocks; a launch that would need more is refused.
   int sms = 0;

@@ -84,3 +84,42 @@ def test_product_path_has_no_oracle_dependency():
     for p in pkg.rglob("*.py"):
         t = p.read_text()
         assert "oracle" not in t.replace("no oracle", ""), p
+
+
+def test_exchange_and_fused_entry_points_validate_arguments(nvlib):
+    """Argument checks that run before any CUDA call (no GPU needed)."""
+    import ctypes
+    lib = nvlib.load()
+    ex = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    # world must be 2..64 and 0 <= rank < world
+    assert lib.nvfp4_exchange_create(0, 1, ctypes.byref(ex), handle) == 2
+    assert lib.nvfp4_exchange_create(2, 2, ctypes.byref(ex), handle) == 2
+    assert lib.nvfp4_exchange_create(0, 65, ctypes.byref(ex), handle) == 2
+    assert lib.nvfp4_exchange_create(0, 2, None, handle) == 2
+    # the exchange cast needs an exchange handle
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(128, 64, 16, 16, 16, 16, 16, None,
+                                                         None, 0, None, 2048, 1, 0, 0, 64,
+                                                         None) == 2
+    # the fused cast needs a workspace, aligned to 4 bytes
+    assert lib.nvfp4_quantize_rht_fused(128, 64, 16, 16, 16, 16, None, None, 0, None, 2048, 1,
+                                        0, None) == 2
+    assert lib.nvfp4_quantize_rht_fused(128, 64, 16, 16, 16, 16, None, None, 0, None, 2048, 1,
+                                        0, 0x1002) == 3
+    # bad shapes are refused before anything is launched
+    assert lib.nvfp4_quantize_rht_fused_noalloc(100, 64, 16, 16, 16, 16, None, None, 0, None,
+                                                2048, 1, 0) == 1
+
+
+def test_ttt_wrapper_swaps_m_and_n(nvlib):
+    """rht_gemm_ttt_wrapper (core.inc:648-678) calls the ntt form with m and n
+    swapped: a shape valid only after the swap passes the checks (and is a
+    no-op when one side is zero)."""
+    lib = nvlib.load()
+    # ntt(m=64, n=128) is invalid (m % 128); the ttt form swaps it to ntt(128, 64)
+    assert lib.nvfp4_rht_gemm_ntt_w_sfc(64, 128, None, 16, 16, 16, 16, None, 0, None, 2048, 0,
+                                        0) == 1
+    assert lib.nvfp4_rht_gemm_ttt(64, 128, None, 16, 16, 16, 16, None, 0, None, 2048, 0,
+                                  0) == 2     # passes the shape check, then refuses NULL A
+    assert lib.nvfp4_rht_gemm_ttt(0, 128, None, None, None, None, None, None, 0, None, 2048, 0,
+                                  0) == 0
