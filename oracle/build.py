@@ -11,8 +11,8 @@ Two outputs:
       libref_fp8.so  TE's scaled FP8 conversions mul_cvt_2x / mul_cvt_4x
                      (ptx.cuh:923-1693), default and _LOOSE_PRECISION builds.
 
-The reference tree is located by $NVFP4_REFERENCE_ROOT (default: the mount
-point used by this build's containers).  On the GPU box the tree is absent and
+The reference tree is located by $NVFP4_REFERENCE_ROOT (default: a directory
+named "reference" beside this repository).  On the GPU box the tree is absent and
 the prebuilt oracle/_ref/*.so files are used as they are.
 """
 from __future__ import annotations
@@ -32,7 +32,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def _ref_root() -> Path:
-    return Path(os.environ.get("NVFP4_REFERENCE_ROOT", "/root/reference"))
+    # default: a "reference" directory beside this repository
+    return Path(os.environ.get("NVFP4_REFERENCE_ROOT", str(HERE.parents[1] / "reference")))
 
 
 def _cutlass_root() -> Path | None:

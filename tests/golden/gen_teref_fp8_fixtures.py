@@ -79,7 +79,7 @@ def run(L, fn, x, dt, width, sw, fmt):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default="gpurun_out")
+    ap.add_argument("--out", default=".")
     a = ap.parse_args()
     L = ref.fp8()
     res = {"scales": SCALES}
