@@ -6,9 +6,11 @@ X (65536 x 14336 bf16, N(0,1) with 0.1% x50 outliers) is split by row blocks
 across the ranks (API view: m = 14336, n = 65536 / N columns per rank), and
 each rank runs
     global-amax pre-pass (nvfp4_amax_bf16)
-    -> NCCL max-allreduce of the scalar (N > 1 only)
-    -> RHT GEMM + NVFP4 cast with stochastic rounding
-       (nvfp4_rht_gemm_ntt_w_sfc_sharded, global RNG coordinates).
+    -> RHT GEMM + NVFP4 cast with stochastic rounding in the full problem's
+       RNG coordinates; for N > 1 the cast kernel itself combines the ranks'
+       amax over NVLink peer memory before its first quantization
+       (nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange; --exchange nccl uses an
+       NCCL int32-MAX all-reduce of the scalar between the two kernels instead).
 `value` is GB/s in the reference's byte convention for the cast
 (2.5625 B per element: 2 read + 0.5 FP4 + 0.0625 SFC, rht_gemm/test_compare.cu:256)
 over all ranks' elements divided by the max-over-ranks step time; the amax
@@ -19,7 +21,17 @@ pass is inside the step.
 --impl reference times the reference's own CPU implementation of the path
 (NaiveReference from rht_gemm/test_correctness.cu, compiled in place into
 oracle/_ref/libref_cpu.so) on the host cores, on a bounded sample of the same
-workload.
+workload; beside it the reference's scalar sr.software quantizer
+(stochastic_rounding/sr.software.cuh) at BASELINE configs 1 and 3.
+
+Besides `value` (exactly K timed steps) the line carries:
+  parity     the step's outputs compared bit for bit with an independent path
+             (N = 1: the fused single-kernel quantizer; N > 1: every rank's
+             shard against the NCCL-exchange path, and rank 0 regenerates the
+             whole input and compares the gathered shards with a single-GPU run)
+  sustained  the same step timed over 200 (N = 1) or 1000 (N > 1) steps
+  cfg4       the cast alone at BASELINE config 4 (5120 x 8192 and the reference
+             test's 8192 x 5120), SR, L2 flushed before every launch
 """
 from __future__ import annotations
 
@@ -250,6 +262,58 @@ class CpuReference:
                 "kind": self.kind, "sample": self.describe(dt)}
 
 
+def sr_software_baseline(reps: int = 3):
+    """The reference's scalar software SR quantizer (stochastic_rounding/
+    sr.software.cuh:100-323, compiled in place into oracle/_ref/libref_cpu.so)
+    on the host cores: cvt_fp32_to_fp4_4x at BASELINE config 1 (2^20 fp32
+    values ~N(0,1)x3) and mul_cvt_bf16_to_fp4_8x at config 3 (16384 x 8192
+    bf16 with 0.1% x50 outliers, scale 1), each on 1 thread and on all
+    threads (median of `reps`).  Bytes counted: input + rbits + FP4 output."""
+    from oracle import oracle, ref
+    if not ref.cpu_available():
+        return {"unavailable": "oracle/_ref/libref_cpu.so not built"}
+    L = ref.cpu()
+    rng = np.random.default_rng(SEED)
+    threads = os.cpu_count() or 1
+    out = {"cores_all": threads}
+    n1 = 1 << 20
+    x1 = (rng.standard_normal(n1) * 3).astype(np.float32)
+    r1 = rng.integers(0, 2**32, n1 // 4, dtype=np.uint32)
+    o1 = np.zeros(n1 // 4, np.uint16)
+    n3 = 16384 * 8192
+    x3 = rng.standard_normal(n3).astype(np.float32)
+    x3[rng.random(n3) < 0.001] *= 50.0
+    x3 = oracle.f32_to_bf16(x3)
+    r3 = rng.integers(0, 2**32, n3 // 4, dtype=np.uint32)
+    o3 = np.zeros(n3 // 8, np.uint32)
+
+    def timed(fn):
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return sorted(ts)[len(ts) // 2]
+
+    for name, n, bpe, call in (
+            ("cfg1_cvt_fp32_to_fp4_4x", n1, 4 + 1 + 0.5,
+             lambda th: L.ref_sw_cvt_fp32_to_fp4_4x_sr(x1.ctypes.data, r1.ctypes.data,
+                                                      o1.ctypes.data, n1 // 4, th)),
+            ("cfg3_mul_cvt_bf16_to_fp4_8x", n3, 2 + 1 + 0.5,
+             lambda th: L.ref_sw_mul_cvt_bf16_to_fp4_8x_sr(x3.ctypes.data, 1.0, r3.ctypes.data,
+                                                          o3.ctypes.data, n3 // 8, th))):
+        res = {"elements": n, "bytes_per_elem": bpe}
+        for th in (1, threads):
+            dt = timed(lambda: call(th))
+            res[f"threads_{th}"] = {"s": round(dt, 5), "elem_per_s": n / dt,
+                                    "GB/s": round(n * bpe / dt / 1e9, 4)}
+        out[name] = res
+    out["kind"] = "reference"
+    out["note"] = ("scalar software SR of the reference (not bit-exact to cvt.rs by design: "
+                   "sr.software.cuh:67-75 hashes the random bits)")
+    return out
+
+
 def bench_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -271,8 +335,9 @@ def bench_reference(args):
         "scaling": "strong",
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(args.gpus),
+        "config": workload_config(args.gpus, args.exchange),
         "elem_per_s": base["elem_per_s"],
+        "sr_software": sr_software_baseline(),
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(base["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -282,13 +347,121 @@ def bench_reference(args):
     return 0
 
 
-def workload_config(n):
+def workload_config(n, exchange="peer"):
+    ex = "none" if n == 1 else exchange
+    how = {"none": "amax pre-pass + RHT GEMM + NVFP4 cast",
+           "peer": "amax pre-pass + RHT GEMM + NVFP4 cast with the ranks' amax combined "
+                   "inside the cast kernel over NVLink peer memory",
+           "nccl": "amax pre-pass + NCCL int32-MAX all-reduce of the amax + RHT GEMM + "
+                   "NVFP4 cast"}[ex]
     return {"workload": "BASELINE cfg5: X 65536x14336 bf16 N(0,1)+0.1% x50 outliers, "
-                        "row-sharded (API m=14336, n=65536/N per rank), amax pre-pass + "
-                        "NCCL max-allreduce + RHT GEMM + NVFP4 cast, stochastic rounding",
+                        f"row-sharded (API m=14336, n=65536/N per rank), {how}, "
+                        "stochastic rounding",
             "m": COLS, "n_total": ROWS, "n_per_rank": ROWS // n, "k_tile_size": 2048,
             "stochastic_rounding": True, "parallelism": f"row-shard x{n}",
+            "amax_exchange": ex,
             "l2": "inputs larger than L2 (per-rank shard >= 235 MB > 126 MB)"}
+
+
+def check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank):
+    """Bit-for-bit check of the step's outputs (C, S and the amax of the
+    last step) against independent paths.  N = 1: the fused single-kernel
+    quantizer.  N > 1: (a) on every rank, the NCCL path -- amax kernel,
+    int32-MAX all-reduce, sharded cast -- on the same shard; (b) rank 0
+    regenerates the whole input from the ranks' seeds, runs the single-GPU
+    amax + cast on it and compares the shards gathered from all ranks."""
+    from fp4_sm120a_b200.sharded import combine_amax
+    m, n, n_total = qz.m, qz.n, qz.n_total
+    C2, S2 = torch.empty_like(C), torch.empty_like(S)
+    am2 = torch.empty(1, dtype=torch.float32, device="cuda")
+    if ws == 1:
+        wsp = nv.fused_workspace()
+        nv.quantize_rht_fused(m, n, A, B, C2, S2, am2, rng_state, wsp, 0, None, 2048,
+                              stochastic_rounding=True)
+        torch.cuda.synchronize()
+        cnt = torch.tensor([int((C2 != C).sum()), int((S2 != S).sum()),
+                            int(not torch.equal(am2.view(torch.int32), amax.view(torch.int32)))],
+                           dtype=torch.int64)
+        return {"checked": True, "fp4_mismatch": int(cnt[0]), "sfc_mismatch": int(cnt[1]),
+                "amax_mismatch": int(cnt[2]),
+                "vs": "fused single-kernel quantizer (nvfp4_quantize_rht_fused), same input"}
+    # (a) this rank's shard through the NCCL exchange path
+    nv.amax_bf16(A, m * n, am2)
+    combine_amax(am2)
+    nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C2, S2, am2, rng_state, qz.n_offset, n_total, 0,
+                                  None, 2048, stochastic_rounding=True)
+    torch.cuda.synchronize()
+    cnt = torch.tensor([int((C2 != C).sum()), int((S2 != S).sum()),
+                        int(not torch.equal(am2.view(torch.int32), amax.view(torch.int32))),
+                        0, 0, 0], dtype=torch.int64, device="cuda")
+    del C2, S2
+    # (b) the gathered shards against one GPU running the whole problem
+    sizes = qz.plan.sizes
+    Cs = [torch.empty((m, sz // 2), dtype=torch.uint8, device="cuda") for sz in sizes]
+    Ss = [torch.empty((m, sz // 16), dtype=torch.uint8, device="cuda") for sz in sizes]
+    dist.all_gather(Cs, C)
+    dist.all_gather(Ss, S)
+    if rank == 0:
+        Af = torch.cat([make_shard(torch, r, sizes[r]) for r in range(ws)])
+        Cf = torch.empty((m, n_total // 2), dtype=torch.uint8, device="cuda")
+        Sf = torch.empty((m, n_total // 16), dtype=torch.uint8, device="cuda")
+        amf = torch.empty(1, dtype=torch.float32, device="cuda")
+        nv.amax_bf16(Af, m * n_total, amf)
+        nv.rht_gemm_ntt_w_sfc(m, n_total, Af, B, Cf, Sf, amf, rng_state, 0, None, 2048,
+                              stochastic_rounding=True)
+        torch.cuda.synchronize()
+        cnt[3] = int((torch.cat(Cs, 1) != Cf).sum())
+        cnt[4] = int((torch.cat(Ss, 1) != Sf).sum())
+        cnt[5] = int(not torch.equal(amf.view(torch.int32), amax.view(torch.int32)))
+        del Af, Cf, Sf
+    del Cs, Ss
+    dist.all_reduce(cnt)
+    c = cnt.tolist()
+    return {"checked": True, "fp4_mismatch": c[0] + c[3], "sfc_mismatch": c[1] + c[4],
+            "amax_mismatch": c[2] + c[5],
+            "detail": {"vs_nccl_path": {"fp4": c[0], "sfc": c[1], "amax": c[2]},
+                       "vs_single_gpu": {"fp4": c[3], "sfc": c[4], "amax": c[5]}},
+            "vs": "single-GPU run of the whole input + NCCL-exchange path on every shard"}
+
+
+def bench_cfg4(torch, nv, peak, reps=50):
+    """The cast alone at BASELINE config 4: m=5120, n=8192 (and the reference
+    test's 8192 x 5120), SR, bf16 N(0,1) with 0.1% x50 outliers; a 512 MB
+    buffer is written before every launch so nothing is served from L2; CUDA
+    events around each launch, median of `reps`."""
+    out = {}
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    for m, n in ((5120, 8192), (8192, 5120)):
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        x = torch.randn(m * n, device="cuda", generator=g)
+        x[torch.rand(m * n, device="cuda", generator=g) < 0.001] *= 50.0
+        A = x.to(torch.bfloat16)
+        del x
+        B = nv.hadamard16(device="cuda")
+        C = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
+        S = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
+        am = torch.empty(1, dtype=torch.float32, device="cuda")
+        rs = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
+        nv.amax_bf16(A, m * n, am)
+        ts = []
+        for i in range(reps + 5):
+            flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            nv.rht_gemm_ntt_w_sfc(m, n, A, B, C, S, am, rs, 0, stream, 2048,
+                                  stochastic_rounding=True)
+            e1.record(stream)
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        us = sorted(a.elapsed_time(b) * 1e3 for a, b in ts[5:])[reps // 2]
+        gbs = (m * n * BYTES_PER_ELEM + RHT_FIXED_BYTES) / (us * 1e-6) / 1e9
+        out[f"m{m}_n{n}"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                             "frac_of_8TBs": round(gbs / NOMINAL_HBM_GBS, 4),
+                             "frac_of_measured": round(gbs / peak, 4)}
+    out["method"] = ("cast only (rht_nvfp4_kernel<SR=1>), L2 flushed by a 512 MB write before "
+                     f"each launch, CUDA events, median of {reps}")
+    return out
 
 
 def bench_ours(args):
@@ -376,16 +549,33 @@ def bench_ours(args):
         step(evs[i])
     torch.cuda.synchronize()
     window(False)
+    # A longer run of the same step, for a steadier figure than K steps give.
+    sus_steps = 200 if ws == 1 else 1000
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    window(True)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for i in range(sus_steps):
+        step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    window(False)
     if ws > 1:
         dist.barrier()
     if sampler:
         sampler.__exit__()
+    if nv.device_error() != 0:
+        raise SystemExit("kernel reported a device timeout")
     ms_total = t0.elapsed_time(t1)
     rht_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-    tt = torch.tensor([ms_total, rht_ms], dtype=torch.float64, device="cuda")
+    tt = torch.tensor([ms_total, rht_ms, s0.elapsed_time(s1)], dtype=torch.float64,
+                      device="cuda")
     if ws > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms_total, rht_ms = tt.tolist()
+    ms_total, rht_ms, sus_ms = tt.tolist()
+    parity = check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank)
     ms_step = ms_total / args.steps
     elems_total = m * n_total
     value = elems_total * BYTES_PER_ELEM / (ms_step * 1e-3) / 1e9
@@ -444,7 +634,7 @@ def bench_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 with 0.1% x50 outliers; BASELINE cfg5 shape)",
-            "config": dict(workload_config(ws), amax_exchange=(args.exchange if ws > 1 else "none")),
+            "config": workload_config(ws, args.exchange),
             "elem_per_s": elems_total / (ms_step * 1e-3),
             "frac_of_8TBs": round(value / NOMINAL_HBM_GBS, 4),
             "step_hbm_gbs": round(elems_total * (BYTES_PER_ELEM + 2.0) / (ms_step * 1e-3) / 1e9,
@@ -465,11 +655,19 @@ def bench_ours(args):
                     "matches_device_path": same,
                     "pipeline": f"HostPipeline, 2 device buffer sets, {e2e_steps} steps timed"},
             "gpu_launches": 2 * args.steps,   # in the timed region (amax + cast per step)
+            "parity": parity,
+            "sustained": {"steps": sus_steps, "ms_per_step": round(sus_ms / sus_steps, 5),
+                          "value": round(elems_total * BYTES_PER_ELEM /
+                                         (sus_ms / sus_steps * 1e-3) / 1e9, 2),
+                          "unit": "GB/s"},
         }
+        if ws == 1:
+            line["cfg4"] = bench_cfg4(torch, nv, peak)
         if ws == 1 and not args.no_cpu_baseline:
             base = CpuReference(float(os.environ.get("NVFP4_CPU_STEP_S", "3"))).baseline(3)
             line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind",
                                                          "sample")}
+            line["cpu_baseline"]["sr_software"] = sr_software_baseline()
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

@@ -29,6 +29,7 @@
 // Every wait is bounded (1 s); a kernel that gives up records an error word
 // and unwinds (drains its TMA loads and MMAs, frees TMEM) instead of hanging.
 #include <cstdint>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -679,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         ws[4 + blockIdx.x] = cta << 16;                    // this block's amax as fp32 bits
         __threadfence();
         if (atomicAdd(p.ws, 1u) == gridDim.x - 1) {
+          __threadfence();   // pairs with the other blocks' fence before their arrival
           uint32_t mx = 0;
           for (uint32_t b = 0; b < gridDim.x; ++b) mx = max(mx, ws[4 + b]);
           ws[2] = mx;
@@ -946,13 +948,16 @@ int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* o
   return NVFP4_OK;
 }
 
+// Per-device, once: the kernel's shared-memory attributes; for the fused
+// kernel also the number of its blocks that fit on one SM (a cooperative
+// launch admits no more).
 template <bool SR, bool FM, bool FUSED>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tb,
-                  const Params& p, int grid, cudaStream_t stream) {
-  static bool attr_set[64] = {false};
+int prepare_kernel(int* per_sm) {
+  static std::atomic<int> attr_set[64];
+  static std::atomic<int> occupancy[64];
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
     if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM, FUSED>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemBytes))
@@ -962,58 +967,87 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMa
                                              cudaFuncAttributePreferredSharedMemoryCarveout,
                                              (int)cudaSharedmemCarveoutMaxShared))
       return cuda_status(e);
-    attr_set[dev] = true;
+    if (dev < 64) attr_set[dev].store(1, std::memory_order_release);
   }
+  if constexpr (FUSED) {
+    // As many blocks per SM as the occupancy calculator reports for this
+    // kernel (one on current drivers, which count the TMEM-allocating kernel
+    // as one per SM, although two run side by side when launched normally).
+    int n = dev < 64 ? occupancy[dev].load(std::memory_order_relaxed) : 0;
+    if (n <= 0) {
+      if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+              &n, rht_nvfp4_kernel<SR, FM, FUSED>, kThreads, kSmemBytes))
+        return cuda_status(e);
+      if (n < 1) return cuda_status(cudaErrorCooperativeLaunchTooLarge);
+      if (dev < 64) occupancy[dev].store(n, std::memory_order_relaxed);
+    }
+    *per_sm = n;
+  } else {
+    *per_sm = 2;
+  }
+  return NVFP4_OK;
+}
+
+template <bool SR, bool FM, bool FUSED>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tb,
+                  const Params& p, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
   if constexpr (!FUSED) {
     // A programmatic dependent of the previous kernel in the stream: its
     // launch and prologue overlap that kernel's tail.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
-      return cuda_status(e);
   } else {
     // The fused kernel's blocks meet at a grid barrier: a cooperative launch
-    // guarantees they are all resident.  It admits as many blocks per SM as
-    // the occupancy calculator reports for this kernel (one on current
-    // drivers, which count the TMEM-allocating kernel as one per SM, although
-    // two run side by side when launched normally).
-    int per_sm = 0, sms = 0;
-    if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, rht_nvfp4_kernel<SR, FM, FUSED>, kThreads, kSmemBytes))
-      return cuda_status(e);
-    if (int e = device_sm_count(&sms)) return e;
-    if (per_sm < 1) return cuda_status(cudaErrorCooperativeLaunchTooLarge);
-    if (grid > per_sm * sms) grid = per_sm * sms;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    // guarantees they are all resident.
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
-      return cuda_status(e);
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
+    return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
+
+struct KernelEntry {
+  int (*prepare)(int*);
+  int (*launch)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const Params&, int,
+                cudaStream_t);
+};
+template <bool SR, bool FM, bool FUSED>
+constexpr KernelEntry entry_for() {
+  return {&prepare_kernel<SR, FM, FUSED>, &launch_kernel<SR, FM, FUSED>};
+}
+KernelEntry kernel_entry(bool sr, bool fm, bool fused) {
+  static constexpr KernelEntry table[8] = {
+      entry_for<false, false, false>(), entry_for<false, true, false>(),
+      entry_for<true, false, false>(),  entry_for<true, true, false>(),
+      entry_for<false, false, true>(),  entry_for<false, true, true>(),
+      entry_for<true, false, true>(),   entry_for<true, true, true>()};
+  return table[(fused ? 4 : 0) + (sr ? 2 : 0) + (fm ? 1 : 0)];
+}
+
+// How the fused kernel's grid-barrier workspace is handled.
+enum class WsMode {
+  kCaller,      // caller-owned workspace; a grid above its capacity is clamped
+  kStaticClear  // the library's static scratch: a grid above its capacity is
+                // refused, and its arrival counter is cleared (a 4-byte
+                // memset on the stream) right before the launch, after every
+                // check has passed
+};
 
 int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
                const float* global_amax, const size_t* rng_state, uint32_t sm_count,
                cudaStream_t stream, int k_tile_size, int sr, int fm, int n_offset, int n_total,
                const unsigned long long* const* ex_peers = nullptr, int ex_rank = 0,
                int ex_world = 1, uint32_t ex_epoch = 0, float* amax_out = nullptr,
-               uint32_t* fused_ws = nullptr) {
+               uint32_t* fused_ws = nullptr, WsMode ws_mode = WsMode::kCaller) {
   if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
@@ -1070,17 +1104,21 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
     grid = p.units;
   }
 
+  const KernelEntry k = kernel_entry(sr, fm, fused);
+  int per_sm = 0;
+  if (int e = k.prepare(&per_sm)) return e;
   if (fused) {
-    if (grid > kMaxFusedCtas) grid = kMaxFusedCtas;
-    if (sr && fm) return launch_kernel<true, true, true>(ta, tc, tb, p, grid, stream);
-    if (sr) return launch_kernel<true, false, true>(ta, tc, tb, p, grid, stream);
-    if (fm) return launch_kernel<false, true, true>(ta, tc, tb, p, grid, stream);
-    return launch_kernel<false, false, true>(ta, tc, tb, p, grid, stream);
+    if (grid > per_sm * sms) grid = per_sm * sms;   // all blocks resident
+    if (grid > kMaxFusedCtas) {
+      if (ws_mode == WsMode::kStaticClear) return NVFP4_ERR_SCRATCH_CAPACITY;
+      grid = kMaxFusedCtas;
+    }
+    if (ws_mode == WsMode::kStaticClear) {
+      if (cudaError_t e = cudaMemsetAsync(fused_ws, 0, sizeof(uint32_t), stream))
+        return cuda_status(e);
+    }
   }
-  if (sr && fm) return launch_kernel<true, true, false>(ta, tc, tb, p, grid, stream);
-  if (sr) return launch_kernel<true, false, false>(ta, tc, tb, p, grid, stream);
-  if (fm) return launch_kernel<false, true, false>(ta, tc, tb, p, grid, stream);
-  return launch_kernel<false, false, false>(ta, tc, tb, p, grid, stream);
+  return k.launch(ta, tc, tb, p, grid, stream);
 }
 
 }  // namespace rht
@@ -1099,12 +1137,15 @@ int cuda_status(cudaError_t e) {
 }
 
 int device_sm_count(int* sms) {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
-  if (dev < 64 && cache[dev] > 0) {
-    *sms = cache[dev];
-    return NVFP4_OK;
+  if (dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) {
+      *sms = c;
+      return NVFP4_OK;
+    }
   }
   int major = 0, minor = 0, count = 0;
   if (cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev))
@@ -1113,7 +1154,7 @@ int device_sm_count(int* sms) {
   if (major != 10 || minor != 0) return NVFP4_ERR_UNSUPPORTED_DEVICE;
   if (cudaError_t e = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev))
     return cuda_status(e);
-  if (dev < 64) cache[dev] = count;
+  if (dev < 64) cache[dev].store(count, std::memory_order_relaxed);
   *sms = count;
   return NVFP4_OK;
 }
@@ -1294,8 +1335,10 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
 namespace {
 static __device__ __align__(256) uint32_t g_fused_scratch[nvfp4::rht::kFusedWsWords];
 
-// Device address of g_fused_scratch on the current device (looked up on the
-// first call per device).
+// Device address of g_fused_scratch on the current device, looked up on the
+// first call per device and kept.  A cudaDeviceReset unloads the module and
+// may move the array, so the kept address is not valid across a reset of a
+// device this library has used.
 int fused_scratch_address(uint32_t** out) {
   static std::mutex mu;
   static uint32_t* addr[64] = {nullptr};
@@ -1318,26 +1361,20 @@ NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, cons
                                                const size_t* rng_state, uint32_t sm_count,
                                                nvfp4_stream_t stream, int k_tile_size,
                                                int stochastic_rounding, int use_fast_math) {
-  // Shape and pointer checks first, so that a refused call enqueues nothing.
+  // Argument checks that need no device come first (rht_launch repeats them).
   if (m < 0 || n < 0) return NVFP4_ERR_INVALID_SHAPE;
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % nvfp4::rht::kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
   if (!A || !B || !C || !SFC) return NVFP4_ERR_INVALID_ARGUMENT;
-  // The static scratch holds one partial amax per block, for at most
-  // kMaxFusedCtas blocks; a launch that would need more is refused.
-  int sms = 0;
-  if (int e = nvfp4::device_sm_count(&sms)) return e;
-  const int want = (sm_count > 0 && (int)sm_count < sms) ? (int)sm_count : sms;
-  if (want > nvfp4::rht::kMaxFusedCtas) return NVFP4_ERR_SCRATCH_CAPACITY;
   uint32_t* scratch = nullptr;
   if (int e = fused_scratch_address(&scratch)) return e;
-  // The arrival count must start at zero; a launch that gave up part-way may
-  // have left it otherwise.  The other words need no clearing.
-  if (cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream))
-    return nvfp4::cuda_status(e);
+  // rht_launch checks shapes, pointers and the grid against the scratch's
+  // capacity first; only a call that passes every check enqueues anything:
+  // a 4-byte memset of the arrival count (a launch that gave up part-way may
+  // have left it nonzero; the other words need no clearing), then the kernel.
   return rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count, (cudaStream_t)stream,
                     k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n, nullptr, 0,
-                    1, 0, amax_out, scratch);
+                    1, 0, amax_out, scratch, nvfp4::rht::WsMode::kStaticClear);
 }
 
 NVFP4_API int nvfp4_quantize_rht_fused_sharded_exchange(

@@ -15,6 +15,7 @@ follows the row-sharding its north-star configuration asks for.
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from datetime import timedelta
 from typing import Callable, Optional
@@ -70,6 +71,21 @@ def combine_amax(local_amax: torch.Tensor, group=None) -> torch.Tensor:
     return local_amax
 
 
+def stream_context(stream):
+    """Make `stream` torch's current stream for the duration of a step.
+
+    The amax kernel, the NCCL all-reduce and the cast must be ordered on ONE
+    stream: torch.distributed enqueues the all-reduce on torch's current
+    stream, so a step given another stream runs entirely inside this context.
+    `stream` may be None (the current stream), a torch.cuda.Stream or a raw
+    cudaStream_t handle."""
+    if stream is None:
+        return contextlib.nullcontext()
+    if not isinstance(stream, torch.cuda.Stream):
+        stream = torch.cuda.ExternalStream(int(stream))
+    return torch.cuda.stream(stream)
+
+
 class ShardedRhtQuantizer:
     """One rank's side of the row-sharded quantization step."""
 
@@ -121,7 +137,13 @@ class ShardedRhtQuantizer:
                  local_amax_fn: Optional[Callable] = None, cast_fn: Optional[Callable] = None):
         """Quantize this rank's shard; returns the global amax tensor.
         local_amax_fn / cast_fn replace the CUDA kernels (tests run the host
-        logic on CPU with them)."""
+        logic on CPU with them).  `stream` (None: torch's current stream) is
+        made the current stream for the whole step, so that the all-reduce of
+        the NCCL exchange is ordered between the amax kernel and the cast."""
+        with stream_context(stream):
+            return self._step(A_shard, B, C, S, amax, stream, local_amax_fn, cast_fn)
+
+    def _step(self, A_shard, B, C, S, amax, stream, local_amax_fn, cast_fn):
         from . import ops
         if amax is None:
             amax = torch.empty(1, dtype=torch.float32, device=A_shard.device)

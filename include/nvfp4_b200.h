@@ -131,8 +131,14 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
  * same inputs and outputs but keeps the grid-barrier scratch in a 4112-byte
  * array built into the library: every GPU that loads the library holds it
  * until the process exits, and no call allocates anything.
- *   - Limit: a launch may use at most 1024 blocks (one per SM is used);
- *     beyond that it returns NVFP4_ERR_SCRATCH_CAPACITY.
+ *   - Limit: a launch may use at most 1024 blocks.  The grid is the
+ *     cooperative launch's co-resident block count (one per SM on a B200,
+ *     148); a grid above 1024 is refused with NVFP4_ERR_SCRATCH_CAPACITY
+ *     before anything is enqueued.
+ *   - A refused call (bad shape, pointer, alignment or capacity) enqueues
+ *     nothing on `stream`.
+ *   - The looked-up address is kept per device; it is not valid after a
+ *     cudaDeviceReset of that device.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - All calls share the one array: calls that may overlap on the GPU (other

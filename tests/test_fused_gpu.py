@@ -71,3 +71,41 @@ def test_fused_full_size_cfg5(nvlib):
     A[torch.rand(m * n, device="cuda", generator=g) < 0.001] *= 50.0
     A = A.to(torch.bfloat16)
     _two_paths(nvlib, m, n, A, True, False)
+
+
+def _cfg_input(m, n, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn(m * n, device="cuda", generator=g)
+    A[torch.rand(m * n, device="cuda", generator=g) < 0.001] *= 50.0
+    return A.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,n", [(5120, 8192), (14336, 65536)])
+def test_fused_vs_reference_te_kernel(nvlib, m, n):
+    """BASELINE configs 4 and 5, SR: the fused amax + cast is bit-exact with
+    the reference's own TE SM100 kernel (hadamard_transform_cast_fusion_core.inc
+    :513-644, compiled in place) given the amax, and its amax equals torch's
+    max of |A| (an amax computed independently of this library)."""
+    from oracle import ref
+    if not ref.gpu_available():
+        pytest.skip("reference GPU library not built")
+    L = ref.gpu()
+    A = _cfg_input(m, n, m + n)
+    B = dev(h16(np.array([1, -1, -1, 1] * 4)))
+    rs = torch.tensor([777, 5], dtype=torch.int64, device="cuda")
+    want_amax = A.float().abs().max().view(1)
+    C = torch.full((m, n // 2), 0xAA, dtype=torch.uint8, device="cuda")
+    S = torch.full((m, n // 16), 0xAA, dtype=torch.uint8, device="cuda")
+    am = torch.full((1,), -1.0, device="cuda")
+    nvlib.quantize_rht_fused(m, n, A, B, C, S, am, rs, nvlib.fused_workspace(), 0, None, 2048,
+                             stochastic_rounding=True)
+    Cr, Sr = torch.zeros_like(C), torch.zeros_like(S)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rc = L.teref_rht_gemm_ntt_w_sfc(m, n, A.data_ptr(), B.data_ptr(), Cr.data_ptr(),
+                                    Sr.data_ptr(), want_amax.data_ptr(), rs.data_ptr(), sms,
+                                    None, 1, 0)
+    torch.cuda.synchronize()
+    assert rc == 0 and nvlib.device_error() == 0
+    assert torch.equal(am.view(torch.int32), want_amax.view(torch.int32)), (am, want_amax)
+    assert torch.equal(S, Sr), f"SFC mismatches: {(S != Sr).sum().item()}"
+    assert torch.equal(C, Cr), f"FP4 byte mismatches: {(C != Cr).sum().item()}"

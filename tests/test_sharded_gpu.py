@@ -52,8 +52,21 @@ def _worker(rank, world, port, q, exchange="nccl", mode="ok", fused=False):
             dist.barrier()
             dist.destroy_process_group()
             return
-        for _ in range(3):      # several steps: epochs advance, slots alternate
-            amax = qz(shard, B, C, S)
+        if mode == "side_stream":
+            # the step runs on a stream that is not torch's current one, which
+            # is kept busy first: the all-reduce must still sit between the
+            # amax kernel and the cast on that stream
+            side = torch.cuda.Stream()
+            with torch.cuda.stream(side):
+                busy = torch.randn(1 << 27, device="cuda")
+                for _ in range(20):
+                    busy.mul_(1.0001)
+            for _ in range(3):
+                amax = qz(shard, B, C, S, stream=side)
+            torch.cuda.current_stream().wait_stream(side)
+        else:
+            for _ in range(3):      # several steps: epochs advance, slots alternate
+                amax = qz(shard, B, C, S)
         Cs = [torch.empty((m, sz // 2), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
         Ss = [torch.empty((m, sz // 16), dtype=torch.uint8, device="cuda") for sz in qz.plan.sizes]
         dist.all_gather(Cs, C)
@@ -99,3 +112,8 @@ def test_peer_exchange_gives_up_when_a_rank_does_not_join():
     res = _run("peer", "dropout")
     assert res[1] == "skipped"
     assert res[0] == 5, res     # kErrTimeoutExchange, recorded instead of a hang
+
+
+def test_two_gpu_nccl_exchange_on_a_non_current_stream():
+    res = _run("nccl", "side_stream")
+    assert res == {0: True, 1: True}, res
