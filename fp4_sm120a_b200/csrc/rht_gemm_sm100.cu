@@ -75,8 +75,9 @@ constexpr uint32_t kOffClc = kOffB + 512;                 // 16 B per response
 constexpr uint32_t kOffBar = kOffClc + 16 * kClcSlots;
 constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots + 1;
 constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
-constexpr uint32_t kOffMisc = kOffTab + 256 * 4;
-constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
+constexpr uint32_t kOffKey = kOffTab + 256 * 4;         // Philox key schedule, 10 x {k0, k1}
+constexpr uint32_t kOffMisc = kOffKey + 128;
+constexpr uint32_t kSmemBytes = kOffMisc + 32 + 1024;   // + alignment slack
 
 // tcgen05 instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B,
 // both MN-major, N = 16, M = 128.
@@ -249,58 +250,164 @@ __device__ __forceinline__ void mul2(float& a, float& b, float s) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
 }
 
-// Quantize one 16-vector in place with TE's epilogue math (core.inc:439-492):
-// optional bf16 round trip, NaN-propagating amax, SFC = E4M3(amax * S_enc/6),
-// scale = min_nanprop(1 / (E4M3^-1(SFC) * S_dec), FLT_MAX) -- looked up in
-// `tab`, which holds that scale for all 256 SFC codes of this launch -- then
-// FP4 E2M1 by cvt.rs (SR) or cvt.rn.  Returns the SFC code.
+// Shared-memory access by 32-bit shared-window address.
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Two E2M1 x4 conversions by stochastic rounding packed into one word (the
+// first four values in the low half).
+__device__ __forceinline__ uint32_t sr_e2m1x8(float x0, float x1, float x2, float x3, float x4,
+                                              float x5, float x6, float x7, uint32_t r0,
+                                              uint32_t r1) {
+  uint32_t w;
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rs.satfinite.e2m1x4.f32 lo, {%4, %3, %2, %1}, %9;\n\t"
+      "cvt.rs.satfinite.e2m1x4.f32 hi, {%8, %7, %6, %5}, %10;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(w)
+      : "f"(x0), "f"(x1), "f"(x2), "f"(x3), "f"(x4), "f"(x5), "f"(x6), "f"(x7), "r"(r0), "r"(r1));
+  return w;
+}
+
+// quant16 (TE's epilogue math, core.inc:439-492) on two adjacent 16-vectors
+// of one row: writes their 32 FP4 codes to `out` (16 bytes) and returns both
+// SFC codes as one 16-bit value, the first vector's in the low byte, from one
+// cvt.rn.satfinite.e4m3x2.  `tab` is the shared-window address of the
+// 256-entry reciprocal-scale table.
 template <bool SR, bool FM>
-__device__ __forceinline__ uint32_t quant16(float* x, float enc_mult, const float* tab, uint4 rb,
-                                            uint32_t& w0, uint32_t& w1) {
+__device__ __forceinline__ uint32_t quant32(float* x, float enc_mult, uint32_t tab, uint4 ra,
+                                            uint4 rb, uint4& out) {
   if constexpr (!FM) {
 #pragma unroll
-    for (int k = 0; k < 16; k += 2) bf16_round_pair(x[k], x[k + 1]);
+    for (int k = 0; k < 32; k += 2) bf16_round_pair(x[k], x[k + 1]);
   }
-  float am = max3_nan(fabsf(x[0]), fabsf(x[1]), fabsf(x[2]));
+  float a0 = max3_nan(fabsf(x[0]), fabsf(x[1]), fabsf(x[2]));
+  float a1 = max3_nan(fabsf(x[16]), fabsf(x[17]), fabsf(x[18]));
 #pragma unroll
-  for (int k = 3; k < 15; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
-  am = fmax_nan(am, fabsf(x[15]));
-  const uint32_t code = e4m3_encode(am * enc_mult);
-  const float acc = tab[code];
+  for (int k = 3; k < 15; k += 2) {
+    a0 = max3_nan(a0, fabsf(x[k]), fabsf(x[k + 1]));
+    a1 = max3_nan(a1, fabsf(x[16 + k]), fabsf(x[17 + k]));
+  }
+  a0 = fmax_nan(a0, fabsf(x[15]));
+  a1 = fmax_nan(a1, fabsf(x[31]));
+  uint32_t h;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(h)
+      : "f"(a1 * enc_mult), "f"(a0 * enc_mult));
+  const float s0 = lds_f32(tab + ((h & 0xFFu) << 2)), s1 = lds_f32(tab + ((h >> 8) << 2));
 #pragma unroll
-  for (int k = 0; k < 16; k += 2) mul2(x[k], x[k + 1], acc);
+  for (int k = 0; k < 16; k += 2) mul2(x[k], x[k + 1], s0);
+#pragma unroll
+  for (int k = 16; k < 32; k += 2) mul2(x[k], x[k + 1], s1);
   if constexpr (SR) {
-    w0 = (uint32_t)sr_e2m1x4(x[0], x[1], x[2], x[3], rb.x) |
-         ((uint32_t)sr_e2m1x4(x[4], x[5], x[6], x[7], rb.y) << 16);
-    w1 = (uint32_t)sr_e2m1x4(x[8], x[9], x[10], x[11], rb.z) |
-         ((uint32_t)sr_e2m1x4(x[12], x[13], x[14], x[15], rb.w) << 16);
+    out.x = sr_e2m1x8(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7], ra.x, ra.y);
+    out.y = sr_e2m1x8(x[8], x[9], x[10], x[11], x[12], x[13], x[14], x[15], ra.z, ra.w);
+    out.z = sr_e2m1x8(x[16], x[17], x[18], x[19], x[20], x[21], x[22], x[23], rb.x, rb.y);
+    out.w = sr_e2m1x8(x[24], x[25], x[26], x[27], x[28], x[29], x[30], x[31], rb.z, rb.w);
   } else {
-    w0 = rn_e2m1x2(x[0], x[1]) | (rn_e2m1x2(x[2], x[3]) << 8) | (rn_e2m1x2(x[4], x[5]) << 16) |
-         (rn_e2m1x2(x[6], x[7]) << 24);
-    w1 = rn_e2m1x2(x[8], x[9]) | (rn_e2m1x2(x[10], x[11]) << 8) |
-         (rn_e2m1x2(x[12], x[13]) << 16) | (rn_e2m1x2(x[14], x[15]) << 24);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = rn_e2m1x2(x[8 * i], x[8 * i + 1]) | (rn_e2m1x2(x[8 * i + 2], x[8 * i + 3]) << 8) |
+             (rn_e2m1x2(x[8 * i + 4], x[8 * i + 5]) << 16) |
+             (rn_e2m1x2(x[8 * i + 6], x[8 * i + 7]) << 24);
+    out = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  return code;
+  return h;
+}
+
+// Philox4x32-10 of the four counters (x0 + i, y, z, 0), i = 0..3, which
+// differ only in their first word and do not carry out of it (x0 + 3 does
+// not wrap).  Their first two rounds share work: round 0 multiplies the
+// common z, round 1 the common first word it produced.  The key schedule
+// {k0[r], k1[r]} is read from shared memory (`keys`, 16 bytes per two rounds).
+__device__ __forceinline__ void philox4_shared(uint32_t x0, uint32_t y, uint32_t z, uint32_t keys,
+                                               uint4 (&out)[4]) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  uint32_t c0[4], c1[4], c2[4], c3[4];
+  uint4 kk = lds128(keys);   // rounds 0 and 1
+  const uint64_t q1 = (uint64_t)M1 * z;
+  const uint32_t s0 = (uint32_t)(q1 >> 32) ^ y ^ kk.x;
+  const uint32_t s1 = (uint32_t)q1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t q0 = (uint64_t)M0 * (x0 + (uint32_t)i);
+    c2[i] = (uint32_t)(q0 >> 32) ^ kk.y;   // ^ w, w = 0
+    c3[i] = (uint32_t)q0;
+  }
+  const uint64_t q0s = (uint64_t)M0 * s0;
+  const uint32_t h0 = (uint32_t)(q0s >> 32), l0 = (uint32_t)q0s;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t qq = (uint64_t)M1 * c2[i];
+    c0[i] = (uint32_t)(qq >> 32) ^ s1 ^ kk.z;
+    c1[i] = (uint32_t)qq;
+    c2[i] = h0 ^ c3[i] ^ kk.w;
+    c3[i] = l0;
+  }
+#pragma unroll
+  for (int rp = 1; rp < 5; ++rp) {
+    kk = lds128(keys + 16 * rp);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t ka = h ? kk.z : kk.x, kb = h ? kk.w : kk.y;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t pa = (uint64_t)M0 * c0[i], pb = (uint64_t)M1 * c2[i];
+        const uint32_t n0 = (uint32_t)(pb >> 32) ^ c1[i] ^ ka;
+        const uint32_t n2 = (uint32_t)(pa >> 32) ^ c3[i] ^ kb;
+        c1[i] = (uint32_t)pb;
+        c3[i] = (uint32_t)pa;
+        c0[i] = n0;
+        c2[i] = n2;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = make_uint4(c0[i], c1[i], c2[i], c3[i]);
 }
 
 // Philox4x32-10 for two consecutive counters (ctr and ctr + 1 in x with
-// carry), with the key schedule precomputed in k0[r], k1[r].
+// carry), with the key schedule read from shared memory as in philox4_shared.
 __device__ __forceinline__ void philox_pair(uint32_t x, uint32_t y, uint32_t z, uint32_t w,
-                                            const uint32_t (&k0)[10], const uint32_t (&k1)[10],
-                                            uint4& ra, uint4& rb) {
+                                            uint32_t keys, uint4& ra, uint4& rb) {
   uint32_t a0 = x, a1 = y, a2 = z, a3 = w;
   uint32_t b0 = x + 1u, b1 = y, b2 = z, b3 = w;
   if (b0 == 0u) { if (++b1 == 0u) { if (++b2 == 0u) ++b3; } }
 #pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint64_t pa0 = (uint64_t)0xD2511F53u * a0, pa1 = (uint64_t)0xCD9E8D57u * a2;
-    const uint64_t pb0 = (uint64_t)0xD2511F53u * b0, pb1 = (uint64_t)0xCD9E8D57u * b2;
-    const uint32_t na0 = (uint32_t)(pa1 >> 32) ^ a1 ^ k0[r];
-    const uint32_t na2 = (uint32_t)(pa0 >> 32) ^ a3 ^ k1[r];
-    const uint32_t nb0 = (uint32_t)(pb1 >> 32) ^ b1 ^ k0[r];
-    const uint32_t nb2 = (uint32_t)(pb0 >> 32) ^ b3 ^ k1[r];
-    a1 = (uint32_t)pa1; a3 = (uint32_t)pa0; a0 = na0; a2 = na2;
-    b1 = (uint32_t)pb1; b3 = (uint32_t)pb0; b0 = nb0; b2 = nb2;
+  for (int rp = 0; rp < 5; ++rp) {
+    const uint4 kk = lds128(keys + 16 * rp);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t ka = h ? kk.z : kk.x, kb = h ? kk.w : kk.y;
+      const uint64_t pa0 = (uint64_t)0xD2511F53u * a0, pa1 = (uint64_t)0xCD9E8D57u * a2;
+      const uint64_t pb0 = (uint64_t)0xD2511F53u * b0, pb1 = (uint64_t)0xCD9E8D57u * b2;
+      const uint32_t na0 = (uint32_t)(pa1 >> 32) ^ a1 ^ ka;
+      const uint32_t na2 = (uint32_t)(pa0 >> 32) ^ a3 ^ kb;
+      const uint32_t nb0 = (uint32_t)(pb1 >> 32) ^ b1 ^ ka;
+      const uint32_t nb2 = (uint32_t)(pb0 >> 32) ^ b3 ^ kb;
+      a1 = (uint32_t)pa1; a3 = (uint32_t)pa0; a0 = na0; a2 = na2;
+      b1 = (uint32_t)pb1; b3 = (uint32_t)pb0; b0 = nb0; b2 = nb2;
+    }
   }
   ra = make_uint4(a0, a1, a2, a3);
   rb = make_uint4(b0, b1, b2, b3);
@@ -630,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ------------------------------ epilogue ----------------------------------
     const int ew = warp - 2;
     const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int slice0 = ew >> 2;       // slices slice0 and slice0 + 2 of each stage
+    const int g = ew >> 2;            // k-block g of each stage: slices 2g, 2g + 1
     const int r = q * 32 + lane;      // row within the 128-row tile
     const bool leader = (ew == 0 && lane == 0);
 
@@ -714,24 +821,43 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float rcp = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
       acc_tab[code] = fmin_nan(rcp, 3.402823466e38f);
     }
+    if constexpr (SR) {
+      // Philox key schedule k_r = seed + r * (0x9E3779B9, 0xBB67AE85), stored
+      // as {k0[r], k1[r]} pairs for 16-byte loads of two rounds at a time
+      const int tid = ew * 32 + lane;
+      if (tid < 10) {
+        const uint64_t seed = p.rng != nullptr ? p.rng[0] : 0ull;
+        uint32_t* kt = reinterpret_cast<uint32_t*>(smem + kOffKey);
+        kt[2 * tid] = (uint32_t)seed + (uint32_t)tid * 0x9E3779B9u;
+        kt[2 * tid + 1] = (uint32_t)(seed >> 32) + (uint32_t)tid * 0xBB67AE85u;
+      }
+    }
     named_bar_sync(2, kEpiThreads);
     const float enc_mult = global_encode_scale(gamax) * (1.0f / 6.0f);
-    uint32_t k0[10], k1[10];
+    const uint32_t tab = sbase + kOffTab;
+    const uint32_t keys = sbase + kOffKey;
     uint32_t olo = 0, ohi = 0;
     if constexpr (SR) {
-      uint64_t seed = 0, offset = 0;
-      if (p.rng != nullptr) {
-        seed = p.rng[0];
-        offset = p.rng[1];
-      }
-#pragma unroll
-      for (int i = 0; i < 10; ++i) {
-        k0[i] = (uint32_t)seed + (uint32_t)i * 0x9E3779B9u;
-        k1[i] = (uint32_t)(seed >> 32) + (uint32_t)i * 0xBB67AE85u;
-      }
+      uint64_t offset = 0;
+      if (p.rng != nullptr) offset = p.rng[1];
       olo = (uint32_t)offset;
       ohi = (uint32_t)(offset >> 32);
     }
+    // A unit's four k-blocks lie in one RNG chunk when K_TILE_MAX is a
+    // multiple of 4 (units start at multiples of 4 k-blocks).
+    const bool chunk_aligned = (p.ktm & 3u) == 0u;
+    // Per-thread constant addresses.  Row r of the 128 x 128 B FP4 staging
+    // tile holds the unit's columns in 16-byte chunks, chunk c at position
+    // c ^ (r % 8) (128-byte swizzle); this warp group writes chunks 4a + 2g + j.
+    const uint32_t c_row = sbase + kOffC + (uint32_t)r * 128u;
+    const uint32_t s_row = sbase + kOffSfc + (uint32_t)r * 16u + (uint32_t)g * 4u;
+    uint32_t c_off[2][2];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        c_off[a][j] = (((uint32_t)(a * 4 + 2 * g + j)) ^ (uint32_t)(r & 7)) * 16u;
+    const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)g * 64u;
     const int sfc_row_bytes = p.n / 16;
 
     uint32_t acc = 0, accph = 0, ucount = 0;
@@ -742,63 +868,77 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t buf = ucount & 1u;
       uint8_t* cst = smem + kOffC + buf * kCTileBytes;
       uint8_t* sst = smem + kOffSfc + buf * kSfcTileBytes;
+      const uint32_t cb = c_row + buf * kCTileBytes;
+      const uint32_t sb = s_row + buf * kSfcTileBytes;
       // TE's RNG coordinates of this unit's first 64-column k-block
       // (core.inc:161-166, 470-475): kb / K_TILE_MAX and kb % K_TILE_MAX.
       const uint32_t kb0 = (uint32_t)((p.n_offset + t.n0) / kSubN);
       const uint32_t chunk0 = p.div_ktm.div(kb0);
       const uint32_t kt0 = kb0 - chunk0 * p.ktm;
-      for (int a = 0; a < t.nacc && ok; ++a) {
-        // The random words depend only on coordinates, so they are generated
-        // before waiting for the accumulator and overlap that wait.
-        uint4 rb[2][2];
+      // TE's generate4() numbers 0..3 of sequence
+      // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
+      // linear_tile = tile_m + tiles_m * chunk, counter (offset, seq, 0), for
+      // this warp group's k-block 2a + g of stage a.  When the unit's four
+      // k-blocks lie in one RNG chunk (K_TILE_MAX a multiple of 4), seq grows
+      // by 256 per block.
+      const uint32_t seq0 = (uint32_t)r +
+                            (kt0 + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk0) * p.ktm) * 256u +
+                            (uint32_t)g * 256u;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int slice = slice0 + 2 * j;
-          const int blk = 2 * a + (slice >> 1);
-          rb[j][0] = make_uint4(0, 0, 0, 0);
-          rb[j][1] = rb[j][0];
-          if constexpr (SR) {
-            // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
-            // linear_tile = tile_m + tiles_m * chunk; the counter
-            // (offset_lo, offset_hi, seq, 0) advanced by 2 * (slice & 1)
-            // gives generate4() numbers (column % 64) / 16 of that sequence.
+      for (int a = 0; a < 2; ++a) {
+        if (a >= t.nacc) break;
+        const int blk = 2 * a + g;
+        // k-block beyond a ragged unit's end: computed on stale TMEM columns
+        // (allocated, never written for this unit) and not stored
+        const bool valid = blk < t.nsub;
+        uint4 rw[4];
+        if constexpr (SR) {
+          // generated before waiting for the accumulator: overlaps the wait
+          uint32_t seq = seq0 + (uint32_t)a * 512u;
+          if (!chunk_aligned) {
             uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
             while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
-            const uint32_t L = (uint32_t)t.tm + (uint32_t)p.tiles_m * chunk;
-            const uint32_t seq = (uint32_t)r + kt * 256u + L * p.ktm * 256u;
-            uint32_t cx = olo + (uint32_t)(slice & 1) * 2u, cy = ohi, cz = seq, cw = 0;
-            if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
-            philox_pair(cx, cy, cz, cw, k0, k1, rb[j][0], rb[j][1]);
+            seq = (uint32_t)r + (kt + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk) * p.ktm) * 256u;
           }
+          if (olo <= 0xFFFFFFFCu) {
+            philox4_shared(olo, ohi, seq, keys, rw);
+          } else {
+            // the counter's first word wraps within the four: carry each
+            // counter separately
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              uint32_t cx = olo + 2u * (uint32_t)j, cy = ohi, cz = seq, cw = 0;
+              if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
+              philox_pair(cx, cy, cz, cw, keys, rw[2 * j], rw[2 * j + 1]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) rw[i] = make_uint4(0, 0, 0, 0);
         }
         if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t ta = t_row + acc * kAccN;
+        uint32_t h0 = 0;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const int slice = slice0 + 2 * j;
-          const int blk = 2 * a + (slice >> 1);
-          const bool valid = blk < t.nsub;
           float v[32];
-          if (valid) {
-            tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccN + slice * 32, v);
-            tc_wait_ld();
-          }
+          tmem_ld_32cols(ta + j * 32, v);
+          tc_wait_ld();
           if (j == 1) {
+            // both slices are in registers: release the accumulator stage
             tc_fence_before();
             __syncwarp();
             mbar_arrive(acce_bar(acc));
           }
-          if (!valid) continue;
-          uint32_t w0, w1, w2, w3;
-          const uint32_t s0 = quant16<SR, FM>(v, enc_mult, acc_tab, rb[j][0], w0, w1);
-          const uint32_t s1 = quant16<SR, FM>(v + 16, enc_mult, acc_tab, rb[j][1], w2, w3);
-          const uint32_t chunk16 = (uint32_t)(a * 4 + slice) ^ (uint32_t)(r & 7);
-          *reinterpret_cast<uint4*>(cst + r * 128 + chunk16 * 16) = make_uint4(w0, w1, w2, w3);
-          *reinterpret_cast<uint16_t*>(sst + r * 16 + a * 8 + slice * 2) =
-              (uint16_t)(s0 | (s1 << 8));
+          uint4 wq;
+          const uint32_t h = quant32<SR, FM>(v, enc_mult, tab, rw[2 * j], rw[2 * j + 1], wq);
+          if (valid) sts128(cb + c_off[a][j], wq);
+          if (j == 0) h0 = h;
+          else if (valid) sts32(sb + (uint32_t)a * 8u, h0 | (h << 16));
         }
         if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
       }

@@ -6,6 +6,10 @@
     python -m fp4_sm120a_b200.profile_case rowwise --m 16384 --n 8192
     python -m fp4_sm120a_b200.profile_case fp8  --groups 67108864
     ... --time 20      # time 20 launches instead (L2 flushed before each)
+    ... --evict-after  # after each launch, read a 512 MB buffer with the amax
+                       # kernel (reads only), so that the dirty lines the launch
+                       # left in L2 are written back inside that kernel, where a
+                       # per-kernel DRAM capture counts them
 
 Each case runs `--launches` launches of one kernel on seeded inputs and exits
 0.  With --time N it prints one JSON line per case with the median launch time
@@ -98,9 +102,18 @@ def main(argv=None) -> int:
     ap.add_argument("--groups", type=int, default=1 << 26)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--time", type=int, default=0)
+    ap.add_argument("--evict-after", action="store_true")
     a = ap.parse_args(argv)
     g = torch.Generator(device="cuda").manual_seed(0)
     f, nbytes, elems = _case(a, g)
+    if a.evict_after:
+        ev = torch.zeros(256 << 20, dtype=torch.bfloat16, device="cuda")
+        ev_out = torch.empty(1, device="cuda")
+        f0 = f
+
+        def f():
+            f0()
+            ops.amax_bf16(ev, ev.numel(), ev_out)
     if a.time:
         flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device="cuda")
         ts = []
