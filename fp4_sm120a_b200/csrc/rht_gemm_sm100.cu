@@ -495,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bfull_bar = bar0 + 8 * (kNumBars - 1);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
+  volatile int* next_unit = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kStages; ++s) {
@@ -513,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bfull_bar, 1);
     for (uint32_t sl = 0; sl < (uint32_t)kClcSlots; ++sl) {
       mbar_init(clcf_bar(sl), 1);
-      mbar_init(clce_bar(sl), 2 + kEpiWarps);   // producer, MMA, one per epilogue warp
+      mbar_init(clce_bar(sl), 3);   // producer, MMA, epilogue warp 0
     }
     *abort_flag = 0u;
     fence_barrier_init();
@@ -947,6 +948,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       // the next unit will overwrite.
       fence_proxy_async_smem();
       if (leader) bulk_wait_read_all();
+      if (p.dynamic && ew == 0) {
+        // Epilogue warp 0 reads the cluster-launch-control response naming
+        // this CTA's next unit, releases the response slot and passes the
+        // unit on to the other epilogue warps through shared memory.
+        const uint32_t j = ucount + 1, sl = clc_slot(j);
+        int nu = -1;
+        if (ok && warp_wait(clcf_bar(sl), clc_parity(j), abort_flag, kErrTimeoutEpilogue)) {
+          nu = clc_decode(clc_resp(sl));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(clce_bar(sl));
+        }
+        if (lane == 0) next_unit[buf] = nu;
+      }
       __syncwarp();
       named_bar_sync(1, kEpiThreads);
       if (!ok || *abort_flag) {
@@ -974,16 +989,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (p.dynamic) {
-        // every lane reads the response; lane 0 releases the slot for the warp
-        const uint32_t j = ucount + 1, sl = clc_slot(j);
-        int nu = -1;
-        if (ok && warp_wait(clcf_bar(sl), clc_parity(j), abort_flag, kErrTimeoutEpilogue)) {
-          nu = clc_decode(clc_resp(sl));
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(clce_bar(sl));
-        }
-        it.jump(p, nu);
+        it.jump(p, next_unit[buf]);
       } else {
         it.next(p);
       }
