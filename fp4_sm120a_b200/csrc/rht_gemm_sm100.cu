@@ -73,7 +73,7 @@ constexpr uint32_t kOffB = kOffSfc + 2 * kSfcTileBytes;
 constexpr int kClcSlots = 4;      // cluster-launch-control response ring
 constexpr uint32_t kOffClc = kOffB + 512;                 // 16 B per response
 constexpr uint32_t kOffBar = kOffClc + 16 * kClcSlots;
-constexpr uint32_t kNumBars = 4 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots + 1;
+constexpr uint32_t kNumBars = 2 * kStages + 2 * kAccStages + 1 + 2 * kClcSlots + 1;
 constexpr uint32_t kOffTab = kOffBar + 8 * kNumBars;    // 256 reciprocal scales
 constexpr uint32_t kOffKey = kOffTab + 256 * 4;         // Philox key schedule, 10 x {k0, k1}
 constexpr uint32_t kOffMisc = kOffKey + 128;
@@ -126,9 +126,9 @@ struct Params {
   int rank, world;
   uint32_t epoch;
   float* amax_out;       // receives the combined amax (block 0), may be null
-  // Fused kernel: grid-barrier workspace, kFusedWsWords 32-bit words:
-  // [0] arrival count, [1] generation, [2] amax bits, [3] unused,
-  // [4 + b] amax bits of block b.  Zeroed once before first use.
+  // Fused kernel: workspace of kFusedWsWords 32-bit words (layout: kWs*
+  // below).  Zeroed once before first use; each launch leaves it ready for
+  // the next.
   uint32_t* ws;
   // 1: the grid has one CTA per work unit and running CTAs take the units of
   // CTAs not yet started through cluster launch control (dynamic balance);
@@ -138,8 +138,18 @@ struct Params {
   int b_tma;
 };
 
-constexpr int kMaxFusedCtas = 1024;
-constexpr int kFusedWsWords = 4 + kMaxFusedCtas;
+constexpr int kMaxUnits = 0x7FFFFFFF;   // work units per launch (32-bit counts)
+// Fused-kernel workspace words.  The unit counters hand out work units
+// (first pass: ascending; second pass: descending).  The second-pass counter
+// and the amax word alternate between two copies by launch generation, so
+// that the next launch's copy can be cleared while this one's is in use.
+constexpr int kWsArrive = 0;   // grid-barrier arrival count
+constexpr int kWsCnt1 = 1;     // first-pass unit counter
+constexpr int kWsCnt2 = 2;     // second-pass unit counters (2 words, by generation parity)
+constexpr int kWsAmax = 4;     // combined amax bits (2 words, by generation parity)
+constexpr int kWsGen = 6;      // grid-barrier generation (launches so far)
+constexpr int kWsClearBytes = 24;   // words 0..5: the ones a fresh start needs at zero
+constexpr int kFusedWsWords = 8;
 
 // The global amax of this launch.  With world > 1: block 0 publishes
 // {epoch, bits of this rank's amax} into slot `rank` of every rank's slot
@@ -181,20 +191,16 @@ __device__ __forceinline__ float launch_amax(const Params& p, float local,
   return am;
 }
 
-// Work units in the persistent schedule: unit u = tm + tiles_m * un covers
-// rows [128 tm, 128 tm + 128) and columns [256 un, 256 un + 256).  Each CTA
-// owns u = blockIdx.x, blockIdx.x + gridDim.x, ... and walks them forward, or
-// backward (the fused kernel's second pass, so that it first re-reads the
-// tiles its first pass read last, while they are still in L2).
+// Work units: unit u = tm + tiles_m * un covers rows [128 tm, 128 tm + 128)
+// and columns [256 un, 256 un + 256).  In the persistent schedule each CTA
+// owns u = blockIdx.x, blockIdx.x + gridDim.x, ...; under cluster launch
+// control it jumps to the unit of the CTA it cancelled.
 struct UnitIter {
   int u, tm, un, step_m, step_n;
-  bool rev;
-  __device__ __forceinline__ void init(const Params& p, bool reverse = false) {
-    rev = reverse;
+  __device__ __forceinline__ void init(const Params& p) {
     step_n = (int)p.div_tiles_m.div(gridDim.x);
     step_m = (int)gridDim.x - step_n * p.tiles_m;
     u = blockIdx.x;
-    if (rev && u < p.units) u += ((p.units - 1 - u) / (int)gridDim.x) * (int)gridDim.x;
     set(p);
   }
   __device__ __forceinline__ void set(const Params& p) {
@@ -206,15 +212,8 @@ struct UnitIter {
     u = nu < 0 ? p.units : nu;
     if (u < p.units) set(p);
   }
-  __device__ __forceinline__ bool valid(const Params& p) const {
-    return rev ? (u >= (int)blockIdx.x && u < p.units) : (u < p.units);
-  }
+  __device__ __forceinline__ bool valid(const Params& p) const { return u < p.units; }
   __device__ __forceinline__ void next(const Params& p) {
-    if (rev) {
-      u -= gridDim.x;
-      if (u >= 0) set(p);
-      return;
-    }
     u += gridDim.x;
     tm += step_m;
     un += step_n;
@@ -225,15 +224,23 @@ struct UnitIter {
 struct Unit {
   int tm, m0, n0, nsub, nacc;
 };
-__device__ __forceinline__ Unit unit_at(const Params& p, const UnitIter& it) {
+__device__ __forceinline__ Unit unit_from(const Params& p, int tm, int un) {
   Unit t;
-  t.tm = it.tm;
-  t.m0 = it.tm * kBM;
-  t.n0 = it.un * kUnitN;
+  t.tm = tm;
+  t.m0 = tm * kBM;
+  t.n0 = un * kUnitN;
   const int rem = (p.n - t.n0) / kSubN;
   t.nsub = rem < 4 ? rem : 4;
   t.nacc = (t.nsub + 1) / 2;
   return t;
+}
+__device__ __forceinline__ Unit unit_at(const Params& p, const UnitIter& it) {
+  return unit_from(p, it.tm, it.un);
+}
+// Unit number u (u < p.units).
+__device__ __forceinline__ Unit unit_of(const Params& p, int u) {
+  const int un = (int)p.div_tiles_m.div((uint32_t)u);
+  return unit_from(p, u - un * p.tiles_m, un);
 }
 
 __device__ __forceinline__ float max3_nan(float a, float b, float c) {
@@ -455,7 +462,167 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
   return __all_sync(0xFFFFFFFFu, ok);
 }
 
-template <bool SR, bool FM, bool FUSED>
+// ---------------------------------------------------------------------------
+// Epilogue building blocks shared by the cast kernels
+// ---------------------------------------------------------------------------
+
+// Per-thread constants of an epilogue thread, set up once per CTA.
+struct EpiThread {
+  int r, g;               // row within the 128-row tile; this warp group's k-block of a stage
+  uint32_t c_row, s_row;  // row r of the FP4 / SFC staging tiles, buffer 0 (shared window)
+  uint32_t c_off[2][2];   // byte offset of chunk 4a + 2g + j within row r (128-byte swizzle)
+  uint32_t t_row;         // TMEM lane r, column 64 g of accumulator stage 0
+  uint32_t tab, keys;     // reciprocal-scale table, Philox key schedule (shared window)
+  float enc_mult;         // S_enc / 6
+  uint32_t olo, ohi;      // Philox counter offset
+  bool chunk_aligned;     // K_TILE_MAX % 4 == 0: a unit's four k-blocks share one RNG chunk
+};
+
+// q: the TMEM lane quarter of this warp; c_tile / s_tile: shared-window
+// addresses of staging buffer 0; tmem: the CTA's (or pipeline's) first
+// accumulator column.
+template <bool SR>
+__device__ __forceinline__ EpiThread epi_setup(const Params& p, int q, int g, int lane,
+                                               uint32_t c_tile, uint32_t s_tile, uint32_t tmem,
+                                               uint32_t tab, uint32_t keys, float gamax) {
+  EpiThread e;
+  e.r = q * 32 + lane;
+  e.g = g;
+  // Row r of the 128 x 128 B FP4 staging tile holds the unit's columns in
+  // 16-byte chunks, chunk c at position c ^ (r % 8) (128-byte swizzle).
+  e.c_row = c_tile + (uint32_t)e.r * 128u;
+  e.s_row = s_tile + (uint32_t)e.r * 16u + (uint32_t)g * 4u;
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      e.c_off[a][j] = (((uint32_t)(a * 4 + 2 * g + j)) ^ (uint32_t)(e.r & 7)) * 16u;
+  e.t_row = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)g * 64u;
+  e.tab = tab;
+  e.keys = keys;
+  e.enc_mult = global_encode_scale(gamax) * (1.0f / 6.0f);
+  e.olo = 0;
+  e.ohi = 0;
+  if constexpr (SR) {
+    uint64_t offset = 0;
+    if (p.rng != nullptr) offset = p.rng[1];
+    e.olo = (uint32_t)offset;
+    e.ohi = (uint32_t)(offset >> 32);
+  }
+  e.chunk_aligned = (p.ktm & 3u) == 0u;
+  return e;
+}
+
+// The epilogue's share of one work unit: for each accumulator stage a, this
+// warp group's k-block 2a + g: TE's Philox words, then the two 32-column
+// slices of TMEM, quantized into the staging buffers `buf`.  Returns false
+// when a wait gave up.
+template <bool SR, bool FM>
+__device__ __forceinline__ bool epi_cast_unit(const Params& p, const Unit& t, const EpiThread& e,
+                                              uint32_t buf, uint32_t accf0, uint32_t acce0,
+                                              uint32_t& acc, uint32_t& accph,
+                                              volatile uint32_t* abort_flag) {
+  const uint32_t cb = e.c_row + buf * kCTileBytes;
+  const uint32_t sb = e.s_row + buf * kSfcTileBytes;
+  // TE's RNG coordinates of this unit's first 64-column k-block
+  // (core.inc:161-166, 470-475): kb / K_TILE_MAX and kb % K_TILE_MAX.
+  const uint32_t kb0 = (uint32_t)((p.n_offset + t.n0) / kSubN);
+  const uint32_t chunk0 = p.div_ktm.div(kb0);
+  const uint32_t kt0 = kb0 - chunk0 * p.ktm;
+  // TE's generate4() numbers 0..3 of sequence
+  // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
+  // linear_tile = tile_m + tiles_m * chunk, counter (offset, seq, 0), for
+  // k-block 2a + g of stage a.  When the unit's four k-blocks lie in one RNG
+  // chunk, seq grows by 256 per block.
+  const uint32_t seq0 = (uint32_t)e.r +
+                        (kt0 + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk0) * p.ktm) * 256u +
+                        (uint32_t)e.g * 256u;
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    if (a >= t.nacc) break;
+    const int blk = 2 * a + e.g;
+    // k-block beyond a ragged unit's end: computed on stale TMEM columns
+    // (allocated, never written for this unit) and not stored
+    const bool valid = blk < t.nsub;
+    uint4 rw[4];
+    if constexpr (SR) {
+      // generated before waiting for the accumulator: overlaps the wait
+      uint32_t seq = seq0 + (uint32_t)a * 512u;
+      if (!e.chunk_aligned) {
+        uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
+        while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
+        seq = (uint32_t)e.r + (kt + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk) * p.ktm) * 256u;
+      }
+      if (e.olo <= 0xFFFFFFFCu) {
+        philox4_shared(e.olo, e.ohi, seq, e.keys, rw);
+      } else {
+        // the counter's first word wraps within the four: carry each counter
+        // separately
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t cx = e.olo + 2u * (uint32_t)j, cy = e.ohi, cz = seq, cw = 0;
+          if (cx < e.olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
+          philox_pair(cx, cy, cz, cw, e.keys, rw[2 * j], rw[2 * j + 1]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rw[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (!warp_wait(accf0 + 8 * acc, accph, abort_flag, kErrTimeoutEpilogue)) return false;
+    tc_fence_after();
+    const uint32_t ta = e.t_row + acc * kAccN;
+    uint32_t h0 = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float v[32];
+      tmem_ld_32cols(ta + j * 32, v);
+      tc_wait_ld();
+      if (j == 1) {
+        // both slices are in registers: release the accumulator stage
+        tc_fence_before();
+        __syncwarp();
+        mbar_arrive(acce0 + 8 * acc);
+      }
+      uint4 wq;
+      const uint32_t h = quant32<SR, FM>(v, e.enc_mult, e.tab, rw[2 * j], rw[2 * j + 1], wq);
+      if (valid) sts128(cb + e.c_off[a][j], wq);
+      if (j == 0) h0 = h;
+      else if (valid) sts32(sb + (uint32_t)a * 8u, h0 | (h << 16));
+    }
+    if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
+  }
+  return true;
+}
+
+// A finished unit leaves the staging buffers: the leader thread issues the
+// TMA store of the FP4 tile, warps 0-3 of the epilogue copy one 16-byte SFC
+// row each.
+__device__ __forceinline__ void epi_store_unit(const Params& p, const Unit& t,
+                                               const CUtensorMap* tmC, uint32_t c_tile,
+                                               const uint8_t* s_tile, int ew, int lane,
+                                               bool leader) {
+  if (leader) {
+    tma_store_2d(tmC, c_tile, t.n0 / 2, t.m0);
+    bulk_commit();
+  }
+  if (ew < 4) {
+    const int row = ew * 32 + lane;
+    uint8_t* dst = p.sfc + (size_t)(t.m0 + row) * (size_t)(p.n / 16) + t.n0 / 16;
+    const uint8_t* src = s_tile + row * 16;
+    const int nbytes = t.nsub * 4;
+    if (p.sfc_vec == 16 && nbytes == 16) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    } else if (p.sfc_vec >= 4) {
+      for (int b = 0; b < nbytes; b += 4)
+        *reinterpret_cast<uint32_t*>(dst + b) = *reinterpret_cast<const uint32_t*>(src + b);
+    } else {
+      for (int b = 0; b < nbytes; ++b) dst[b] = src[b];
+    }
+  }
+}
+
+template <bool SR, bool FM>
 __global__ void __launch_bounds__(kThreads, 2)
     rht_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmC,
@@ -477,14 +644,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto accf_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + a); };
   auto acce_bar = [&](uint32_t a) { return bar0 + 8 * (2 * kStages + kAccStages + a); };
   const uint32_t drain_bar = bar0 + 8 * (2 * kStages + 2 * kAccStages);
-  // first pass of the fused kernel: its own ring barriers over the same stages
-  auto full1_bar = [&](uint32_t s) { return bar0 + 8 * (2 * kStages + 2 * kAccStages + 1 + s); };
-  auto empty1_bar = [&](uint32_t s) {
-    return bar0 + 8 * (3 * kStages + 2 * kAccStages + 1 + s);
-  };
-  auto clcf_bar = [&](uint32_t s) { return bar0 + 8 * (4 * kStages + 2 * kAccStages + 1 + s); };
+  auto clcf_bar = [&](uint32_t s) { return bar0 + 8 * (2 * kStages + 2 * kAccStages + 1 + s); };
   auto clce_bar = [&](uint32_t s) {
-    return bar0 + 8 * (4 * kStages + 2 * kAccStages + 1 + kClcSlots + s);
+    return bar0 + 8 * (2 * kStages + 2 * kAccStages + 1 + kClcSlots + s);
   };
   auto clc_resp = [&](uint32_t s) { return sbase + kOffClc + 16 * s; };
   // Unit number j >= 1 of this CTA under the dynamic schedule: the response of
@@ -507,10 +669,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(acce_bar(a), kEpiThreads);   // every epilogue thread arrives
     }
     mbar_init(drain_bar, 1);
-    for (uint32_t st = 0; st < kStages; ++st) {
-      mbar_init(full1_bar(st), 1);
-      mbar_init(empty1_bar(st), kEpiThreads);
-    }
     mbar_init(bfull_bar, 1);
     for (uint32_t sl = 0; sl < (uint32_t)kClcSlots; ++sl) {
       mbar_init(clcf_bar(sl), 1);
@@ -557,45 +715,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_expect_tx(bfull_bar, 512);
         tma_load_4d(sbase + kOffB, &tmB, bfull_bar);
       }
-      if constexpr (FUSED) {
-        // First pass: the same tiles, forward, for the epilogue's amax; its
-        // own barriers (full1 / empty1) over the same ring stages.
-        uint32_t st1 = 0, ph1 = 0, n1 = 0;
-        UnitIter it1;
-        for (it1.init(p); it1.valid(p) && ok; it1.next(p)) {
-          const Unit t = unit_at(p, it1);
-          for (int s = 0; s < t.nsub; ++s) {
-            if (!mbar_wait_bounded(empty1_bar(st1), ph1 ^ 1u, abort_flag, kWaitLimitNs,
-                                   kErrTimeoutProducer, &g_device_error_word)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(full1_bar(st1), kStageBytes);
-            const uint32_t dst = sbase + kOffA + st1 * kStageBytes;
-            const int y = t.n0 + s * kSubN;
-            tma_load_2d(dst, &tmA, full1_bar(st1), t.m0, y);
-            tma_load_2d(dst + kHalfBytes, &tmA, full1_bar(st1), t.m0 + 64, y);
-            ++n1;
-            if (++st1 == kStages) { st1 = 0; ph1 ^= 1u; }
-          }
-        }
-        // Every first-pass load lands (bounded, whatever happened), then the
-        // second pass reuses a stage only after the epilogue has read it.
-        const uint32_t pend = n1 < (uint32_t)kStages ? n1 : (uint32_t)kStages;
-        volatile uint32_t never = 0u;
-        for (uint32_t i = 0; i < pend; ++i) {
-          if (st1 == 0) { st1 = kStages - 1; ph1 ^= 1u; } else { --st1; }
-          mbar_wait_bounded(full1_bar(st1), ph1, &never, kWaitLimitNs, kErrTimeoutDrain,
-                            &g_device_error_word);
-          if (ok && !mbar_wait_bounded(empty1_bar(st1), ph1, abort_flag, kWaitLimitNs,
-                                       kErrTimeoutProducer, &g_device_error_word))
-            ok = false;
-        }
-      }
       UnitIter it;
       uint32_t k = 0;               // index of the current unit
       bool pending = false;         // a cancel request whose response is unread
-      for (it.init(p, FUSED); it.valid(p) && ok;) {
+      for (it.init(p); it.valid(p) && ok;) {
         if (p.dynamic) {
           // request the unit after this one while this one streams in
           const uint32_t j = k + 1, sl = clc_slot(j);
@@ -676,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         ok = false;
       UnitIter it;
       uint32_t k = 0;
-      for (it.init(p, FUSED); it.valid(p) && ok;) {
+      for (it.init(p); it.valid(p) && ok;) {
         const Unit t = unit_at(p, it);
         for (int a = 0; a < t.nacc && ok; ++a) {
           if (!mbar_wait_bounded(acce_bar(acc), accph ^ 1u, abort_flag, kWaitLimitNs,
@@ -739,81 +862,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int ew = warp - 2;
     const int q = warp & 3;           // TMEM lane quarter this warp may access
     const int g = ew >> 2;            // k-block g of each stage: slices 2g, 2g + 1
-    const int r = q * 32 + lane;      // row within the 128-row tile
     const bool leader = (ew == 0 && lane == 0);
 
     // The launch's global amax (possibly exchanged with the other GPUs; the
     // producer and MMA warps already stream in meanwhile), then the
     // reciprocal scale of every SFC code:
     // min_nanprop(1 / (E4M3^-1(code) * S_dec), FLT_MAX), accurate or rcp.approx.
-    if constexpr (FUSED) {
-      // First pass: NaN-propagating max of |A| over this CTA's tiles as they
-      // stream through the ring (unsigned max of the bf16 magnitude bits),
-      // then a grid barrier on the workspace combines the CTAs.
-      uint32_t gen = 0;
-      if (leader) gen = ld_acquire_gpu_u32(p.ws + 1);   // before this block arrives
-      uint32_t m2 = 0, st1 = 0, ph1 = 0;
-      bool ok1 = true;
-      const int tid = ew * 32 + lane;                   // 32 bytes of each 16 KiB stage
-      UnitIter it1;
-      for (it1.init(p); it1.valid(p) && ok1; it1.next(p)) {
-        const Unit t = unit_at(p, it1);
-        for (int s = 0; s < t.nsub; ++s) {
-          if (!warp_wait(full1_bar(st1), ph1, abort_flag, kErrTimeoutEpilogue)) {
-            ok1 = false;
-            break;
-          }
-#pragma unroll
-          for (int j = 0; j < (int)(kStageBytes / (32 * kEpiThreads)); ++j) {
-            const uint4* src = reinterpret_cast<const uint4*>(smem + kOffA + st1 * kStageBytes) +
-                               2 * (tid + j * kEpiThreads);
-            const uint4 x = src[0], y = src[1];
-            m2 = __vmaxu2(m2, x.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.y & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, x.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, x.w & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, y.x & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.y & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, y.z & 0x7FFF7FFFu); m2 = __vmaxu2(m2, y.w & 0x7FFF7FFFu);
-          }
-          mbar_arrive(empty1_bar(st1));
-          if (++st1 == kStages) { st1 = 0; ph1 ^= 1u; }
-        }
-      }
-      const uint32_t mw = __reduce_max_sync(0xFFFFFFFFu, max(m2 & 0xFFFFu, m2 >> 16));
-      uint32_t* red = reinterpret_cast<uint32_t*>(acc_tab);   // free until the table is built
-      if (lane == 0) red[ew] = mw;
-      named_bar_sync(2, kEpiThreads);
-      if (leader) {
-        uint32_t cta = 0;
-        for (int w = 0; w < kEpiWarps; ++w) cta = max(cta, red[w]);
-        volatile uint32_t* ws = p.ws;
-        ws[4 + blockIdx.x] = cta << 16;                    // this block's amax as fp32 bits
-        __threadfence();
-        if (atomicAdd(p.ws, 1u) == gridDim.x - 1) {
-          __threadfence();   // pairs with the other blocks' fence before their arrival
-          uint32_t mx = 0;
-          for (uint32_t b = 0; b < gridDim.x; ++b) mx = max(mx, ws[4 + b]);
-          ws[2] = mx;
-          ws[0] = 0u;                                      // ready for the next launch
-          __threadfence();
-          atomicAdd(p.ws + 1, 1u);                         // release the grid
-        } else {
-          const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire_gpu_u32(p.ws + 1) == gen) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs || *abort_flag) {
-              *abort_flag = 1u;
-              atomicCAS(&g_device_error_word, 0u, (uint32_t)kErrTimeoutGridBarrier);
-              break;
-            }
-          }
-        }
-        __threadfence();
-        const float local = __uint_as_float(ws[2]);
-        const float g = launch_amax(p, local, abort_flag, kWaitLimitNs);
-        if (p.world <= 1 && blockIdx.x == 0 && p.amax_out != nullptr) *p.amax_out = g;
-        *s_amax = g;
-      }
-    } else {
-      if (leader) *s_amax = launch_amax(p, *p.amax, abort_flag, kWaitLimitNs);
-    }
+    if (leader) *s_amax = launch_amax(p, *p.amax, abort_flag, kWaitLimitNs);
     named_bar_sync(2, kEpiThreads);
     const float gamax = *s_amax;
     if (ew * 32 + lane < 256) {
@@ -834,115 +889,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     named_bar_sync(2, kEpiThreads);
-    const float enc_mult = global_encode_scale(gamax) * (1.0f / 6.0f);
-    const uint32_t tab = sbase + kOffTab;
-    const uint32_t keys = sbase + kOffKey;
-    uint32_t olo = 0, ohi = 0;
-    if constexpr (SR) {
-      uint64_t offset = 0;
-      if (p.rng != nullptr) offset = p.rng[1];
-      olo = (uint32_t)offset;
-      ohi = (uint32_t)(offset >> 32);
-    }
-    // A unit's four k-blocks lie in one RNG chunk when K_TILE_MAX is a
-    // multiple of 4 (units start at multiples of 4 k-blocks).
-    const bool chunk_aligned = (p.ktm & 3u) == 0u;
-    // Per-thread constant addresses.  Row r of the 128 x 128 B FP4 staging
-    // tile holds the unit's columns in 16-byte chunks, chunk c at position
-    // c ^ (r % 8) (128-byte swizzle); this warp group writes chunks 4a + 2g + j.
-    const uint32_t c_row = sbase + kOffC + (uint32_t)r * 128u;
-    const uint32_t s_row = sbase + kOffSfc + (uint32_t)r * 16u + (uint32_t)g * 4u;
-    uint32_t c_off[2][2];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-        c_off[a][j] = (((uint32_t)(a * 4 + 2 * g + j)) ^ (uint32_t)(r & 7)) * 16u;
-    const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)g * 64u;
-    const int sfc_row_bytes = p.n / 16;
+    const EpiThread e = epi_setup<SR>(p, q, g, lane, sbase + kOffC, sbase + kOffSfc, tmem_base,
+                                      sbase + kOffTab, sbase + kOffKey, gamax);
 
     uint32_t acc = 0, accph = 0, ucount = 0;
     bool ok = true;
     UnitIter it;
-    for (it.init(p, FUSED); it.valid(p); ++ucount) {
+    for (it.init(p); it.valid(p); ++ucount) {
       const Unit t = unit_at(p, it);
       const uint32_t buf = ucount & 1u;
-      uint8_t* cst = smem + kOffC + buf * kCTileBytes;
-      uint8_t* sst = smem + kOffSfc + buf * kSfcTileBytes;
-      const uint32_t cb = c_row + buf * kCTileBytes;
-      const uint32_t sb = s_row + buf * kSfcTileBytes;
-      // TE's RNG coordinates of this unit's first 64-column k-block
-      // (core.inc:161-166, 470-475): kb / K_TILE_MAX and kb % K_TILE_MAX.
-      const uint32_t kb0 = (uint32_t)((p.n_offset + t.n0) / kSubN);
-      const uint32_t chunk0 = p.div_ktm.div(kb0);
-      const uint32_t kt0 = kb0 - chunk0 * p.ktm;
-      // TE's generate4() numbers 0..3 of sequence
-      // seq = row + k_tile * 256 + linear_tile * K_TILE_MAX * 256 with
-      // linear_tile = tile_m + tiles_m * chunk, counter (offset, seq, 0), for
-      // this warp group's k-block 2a + g of stage a.  When the unit's four
-      // k-blocks lie in one RNG chunk (K_TILE_MAX a multiple of 4), seq grows
-      // by 256 per block.
-      const uint32_t seq0 = (uint32_t)r +
-                            (kt0 + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk0) * p.ktm) * 256u +
-                            (uint32_t)g * 256u;
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        if (a >= t.nacc) break;
-        const int blk = 2 * a + g;
-        // k-block beyond a ragged unit's end: computed on stale TMEM columns
-        // (allocated, never written for this unit) and not stored
-        const bool valid = blk < t.nsub;
-        uint4 rw[4];
-        if constexpr (SR) {
-          // generated before waiting for the accumulator: overlaps the wait
-          uint32_t seq = seq0 + (uint32_t)a * 512u;
-          if (!chunk_aligned) {
-            uint32_t kt = kt0 + (uint32_t)blk, chunk = chunk0;
-            while (kt >= p.ktm) { kt -= p.ktm; ++chunk; }
-            seq = (uint32_t)r + (kt + ((uint32_t)t.tm + (uint32_t)p.tiles_m * chunk) * p.ktm) * 256u;
-          }
-          if (olo <= 0xFFFFFFFCu) {
-            philox4_shared(olo, ohi, seq, keys, rw);
-          } else {
-            // the counter's first word wraps within the four: carry each
-            // counter separately
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              uint32_t cx = olo + 2u * (uint32_t)j, cy = ohi, cz = seq, cw = 0;
-              if (cx < olo) { if (++cy == 0u) { if (++cz == 0u) ++cw; } }
-              philox_pair(cx, cy, cz, cw, keys, rw[2 * j], rw[2 * j + 1]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) rw[i] = make_uint4(0, 0, 0, 0);
-        }
-        if (!warp_wait(accf_bar(acc), accph, abort_flag, kErrTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t ta = t_row + acc * kAccN;
-        uint32_t h0 = 0;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float v[32];
-          tmem_ld_32cols(ta + j * 32, v);
-          tc_wait_ld();
-          if (j == 1) {
-            // both slices are in registers: release the accumulator stage
-            tc_fence_before();
-            __syncwarp();
-            mbar_arrive(acce_bar(acc));
-          }
-          uint4 wq;
-          const uint32_t h = quant32<SR, FM>(v, enc_mult, tab, rw[2 * j], rw[2 * j + 1], wq);
-          if (valid) sts128(cb + c_off[a][j], wq);
-          if (j == 0) h0 = h;
-          else if (valid) sts32(sb + (uint32_t)a * 8u, h0 | (h << 16));
-        }
-        if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
-      }
+      // (ok is true here: a unit after a failed wait ends the walk below)
+      ok = epi_cast_unit<SR, FM>(p, t, e, buf, accf_bar(0), acce_bar(0), acc, accph, abort_flag);
       // One barrier per unit among the epilogue warps.  Before it, the leader
       // waits until the previous TMA store has read its staging buffer, which
       // the next unit will overwrite.
@@ -970,24 +927,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         else it.next(p);
         continue;
       }
-      if (leader) {
-        tma_store_2d(&tmC, smem_addr(cst), t.n0 / 2, t.m0);
-        bulk_commit();
-      }
-      if (ew < 4) {
-        const int row = ew * 32 + lane;
-        uint8_t* dst = p.sfc + (size_t)(t.m0 + row) * sfc_row_bytes + t.n0 / 16;
-        const uint8_t* src = sst + row * 16;
-        const int nbytes = t.nsub * 4;
-        if (p.sfc_vec == 16 && nbytes == 16) {
-          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-        } else if (p.sfc_vec >= 4) {
-          for (int b = 0; b < nbytes; b += 4)
-            *reinterpret_cast<uint32_t*>(dst + b) = *reinterpret_cast<const uint32_t*>(src + b);
-        } else {
-          for (int b = 0; b < nbytes; ++b) dst[b] = src[b];
-        }
-      }
+      epi_store_unit(p, t, &tmC, sbase + kOffC + buf * kCTileBytes,
+                     smem + kOffSfc + buf * kSfcTileBytes, ew, lane, leader);
       if (p.dynamic) {
         it.jump(p, next_unit[buf]);
       } else {
@@ -1003,6 +944,451 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Fused amax + cast (one launch): rht_fused_kernel
+//
+// One CTA per SM (the cooperative launch's co-residency guarantee covers the
+// grid barrier) holding two independent pipelines ("halves"), each the same
+// producer / MMA / 8-warp epilogue arrangement as rht_nvfp4_kernel with its
+// own shared-memory ring, barriers and 256 TMEM columns -- the SM's resources
+// are used as by two rht_nvfp4_kernel CTAs.
+//   pass 1   the producers stream the tiles of units handed out by a global
+//            counter (ascending); the epilogue warps take the NaN-propagating
+//            max of |A| straight from the shared-memory stages
+//   barrier  the CTAs combine their maxima (and, with world > 1, the ranks')
+//   pass 2   the cast, over units handed out in descending order, so that the
+//            tiles pass 1 read last are re-read while still in L2; the
+//            producer and MMA warps start it before the barrier, only the
+//            epilogue needs the amax
+// ---------------------------------------------------------------------------
+namespace fz {
+constexpr int kHalves = 2;
+constexpr int kThreadsF = kHalves * kThreads;
+constexpr int kQSlots = 4;      // second-pass unit slots per half
+// offsets within a half's region
+constexpr uint32_t kA = 0;
+constexpr uint32_t kC = kA + kStages * kStageBytes;
+constexpr uint32_t kSfc = kC + 2 * kCTileBytes;
+constexpr uint32_t kEnd = kSfc + 2 * kSfcTileBytes;   // pass-1 end marker, one word per stage
+constexpr uint32_t kQ = kEnd + 4 * kStages;            // pass-2 unit slots
+constexpr uint32_t kNext = kQ + 4 * kQSlots;           // next unit for the epilogue warps (2 words)
+constexpr uint32_t kBar = kNext + 8;
+// full, empty, full1, empty1 per stage; accf, acce per accumulator stage;
+// drain; qf, qe per unit slot
+constexpr uint32_t kNumBarsH = 4 * kStages + 2 * kAccStages + 1 + 2 * kQSlots;
+constexpr uint32_t kRegion = ((kBar + 8 * kNumBarsH) + 1023u) & ~1023u;
+// shared by the halves
+constexpr uint32_t kB = kHalves * kRegion;     // 16 x 16 bf16
+constexpr uint32_t kTab = kB + 512;            // 256 reciprocal scales
+constexpr uint32_t kKey = kTab + 1024;         // Philox key schedule
+constexpr uint32_t kBfull = kKey + 128;        // B's barrier
+constexpr uint32_t kMisc = kBfull + 8;         // TMEM base, abort flag, amax
+constexpr uint32_t kRed = kMisc + 16;          // per-warp maxima, 16 words
+constexpr uint32_t kSmemBytes = kRed + 64 + 1024;   // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "fused kernel shared memory");
+static_assert(kEnd % 16 == 0 && kBar % 8 == 0, "fused kernel layout");
+}  // namespace fz
+
+template <bool SR, bool FM>
+__global__ void __launch_bounds__(fz::kThreadsF, 1)
+    rht_fused_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmC,
+                     const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int half = warp / (kThreads / 32);
+  const int lw = warp - half * (kThreads / 32);   // warp within the half: 0 producer, 1 MMA
+  uint8_t* hs = smem + half * fz::kRegion;
+  const uint32_t hbase = sbase + half * fz::kRegion;
+
+  const uint32_t bar0 = hbase + fz::kBar;
+  auto full_bar = [&](uint32_t s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](uint32_t s) { return bar0 + 8 * (kStages + s); };
+  auto full1_bar = [&](uint32_t s) { return bar0 + 8 * (2 * kStages + s); };
+  auto empty1_bar = [&](uint32_t s) { return bar0 + 8 * (3 * kStages + s); };
+  const uint32_t accf0 = bar0 + 8 * (4 * kStages);
+  const uint32_t acce0 = accf0 + 8 * kAccStages;
+  const uint32_t drain_bar = acce0 + 8 * kAccStages;
+  auto qf_bar = [&](uint32_t s) { return drain_bar + 8 * (1 + s); };
+  auto qe_bar = [&](uint32_t s) { return drain_bar + 8 * (1 + fz::kQSlots + s); };
+  const uint32_t bfull_bar = sbase + fz::kBfull;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + fz::kMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + fz::kMisc + 4);
+  float* s_amax = reinterpret_cast<float*>(smem + fz::kMisc + 8);
+  volatile uint32_t* end_flag = reinterpret_cast<volatile uint32_t*>(hs + fz::kEnd);
+  volatile int* qslot = reinterpret_cast<volatile int*>(hs + fz::kQ);
+  volatile int* next_unit = reinterpret_cast<volatile int*>(hs + fz::kNext);
+
+  if (lw == 0 && lane == 0) {
+    // thread 0 of each half: that half's barriers
+    for (uint32_t s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+      mbar_init(full1_bar(s), 1);
+      mbar_init(empty1_bar(s), kEpiThreads);
+    }
+    for (uint32_t a = 0; a < kAccStages; ++a) {
+      mbar_init(accf0 + 8 * a, 1);
+      mbar_init(acce0 + 8 * a, kEpiThreads);
+    }
+    mbar_init(drain_bar, 1);
+    for (uint32_t s = 0; s < (uint32_t)fz::kQSlots; ++s) {
+      mbar_init(qf_bar(s), 1);
+      mbar_init(qe_bar(s), 2);   // MMA, epilogue warp 0
+    }
+    if (half == 0) {
+      mbar_init(bfull_bar, 1);
+      *abort_flag = 0u;
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmC);
+    if (p.b_tma) prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    if (!p.b_tma) {
+      // B into shared memory in the canonical no-swizzle MN-major layout
+      uint16_t* sb = reinterpret_cast<uint16_t*>(smem + fz::kB);
+      for (int idx = lane; idx < 256; idx += 32) {
+        const int k = idx >> 4, c = idx & 15;
+        const uint32_t off = (c & 7) * 2 + (k & 7) * 16 + (c >> 3) * 128 + (k >> 3) * 256;
+        sb[off >> 1] = p.B[idx];
+      }
+      fence_proxy_async_smem();
+    }
+    tmem_alloc(smem_addr(tmem_holder), fz::kHalves * kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_all = *tmem_holder;
+  const uint32_t tmem_base = tmem_all + (uint32_t)half * kTmemCols;
+  const uint32_t units = (uint32_t)p.units;
+
+  if (lw == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      // The launch's generation selects its second-pass counter; it is read
+      // before this CTA can reach the grid barrier, which advances it.
+      const uint32_t gen = ld_acquire_gpu_u32(p.ws + kWsGen);
+      bool ok = true;
+      if (half == 0 && p.b_tma) {
+        mbar_arrive_expect_tx(bfull_bar, 512);
+        tma_load_4d(sbase + fz::kB, &tmB, bfull_bar);
+      }
+      // Pass 1: units from the first counter; after the last, an end marker
+      // posted on the next stage.
+      uint32_t st = 0, ph = 0, posted = 0;
+      uint32_t u_next = atomicAdd(p.ws + kWsCnt1, 1u);
+      while (ok) {
+        // the unit after this one is requested before this one's loads
+        const uint32_t u = u_next;
+        const bool last = u >= units;
+        if (!last) u_next = atomicAdd(p.ws + kWsCnt1, 1u);
+        Unit t;
+        t.nsub = 1;
+        if (!last) t = unit_of(p, (int)u);
+        for (int s = 0; s < t.nsub; ++s) {
+          if (!mbar_wait_bounded(empty1_bar(st), ph ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutProducer, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          if (last) {
+            end_flag[st] = 1u;
+            mbar_arrive(full1_bar(st));
+          } else {
+            end_flag[st] = 0u;
+            mbar_arrive_expect_tx(full1_bar(st), kStageBytes);
+            const uint32_t dst = hbase + fz::kA + st * kStageBytes;
+            const int y = t.n0 + s * kSubN;
+            tma_load_2d(dst, &tmA, full1_bar(st), t.m0, y);
+            tma_load_2d(dst + kHalfBytes, &tmA, full1_bar(st), t.m0 + 64, y);
+          }
+          ++posted;
+          if (++st == kStages) { st = 0; ph ^= 1u; }
+        }
+        if (last) break;
+      }
+      // Every first-pass posting completes (bounded, whatever happened), and
+      // the second pass reuses a stage only after the epilogue has read it.
+      {
+        const uint32_t pend = posted < (uint32_t)kStages ? posted : (uint32_t)kStages;
+        volatile uint32_t never = 0u;
+        for (uint32_t i = 0; i < pend; ++i) {
+          if (st == 0) { st = kStages - 1; ph ^= 1u; } else { --st; }
+          mbar_wait_bounded(full1_bar(st), ph, &never, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
+          if (ok && !mbar_wait_bounded(empty1_bar(st), ph, abort_flag, kWaitLimitNs,
+                                       kErrTimeoutProducer, &g_device_error_word))
+            ok = false;
+        }
+      }
+      // Pass 2: units in descending order, each posted to the MMA and the
+      // epilogue one unit ahead of its loads.
+      uint32_t* cnt2 = p.ws + kWsCnt2 + (gen & 1u);
+      auto fetch = [&]() -> int {
+        const uint32_t u = atomicAdd(cnt2, 1u);
+        return u < units ? (int)(units - 1u - u) : -1;
+      };
+      auto post = [&](uint32_t j, int unit) -> bool {
+        const uint32_t sl = j % (uint32_t)fz::kQSlots, par = (j / (uint32_t)fz::kQSlots) & 1u;
+        if (!mbar_wait_bounded(qe_bar(sl), par ^ 1u, abort_flag, kWaitLimitNs,
+                               kErrTimeoutProducer, &g_device_error_word))
+          return false;
+        qslot[sl] = unit;
+        mbar_arrive(qf_bar(sl));
+        return true;
+      };
+      uint32_t stage = 0, phase = 0, issued = 0, j = 0;
+      int cur = ok ? fetch() : -1;
+      if (!post(0, cur)) ok = false;
+      while (ok && cur >= 0) {
+        const int nxt = fetch();
+        if (!post(j + 1, nxt)) {
+          ok = false;
+          break;
+        }
+        const Unit t = unit_of(p, cur);
+        for (int s = 0; s < t.nsub; ++s) {
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutProducer, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
+          const uint32_t dst = hbase + fz::kA + stage * kStageBytes;
+          const int y = t.n0 + s * kSubN;
+          tma_load_2d(dst, &tmA, full_bar(stage), t.m0, y);
+          tma_load_2d(dst + kHalfBytes, &tmA, full_bar(stage), t.m0 + 64, y);
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        cur = nxt;
+        ++j;
+      }
+      if (!ok) {
+        // Let the loads already in flight land before the CTA exits.
+        volatile uint32_t never = 0u;
+        if (half == 0 && p.b_tma)
+          mbar_wait_bounded(bfull_bar, 0, &never, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
+        uint32_t st2 = stage, ph2 = phase;
+        const uint32_t n_pending = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+        for (uint32_t i = 0; i < n_pending; ++i) {
+          if (st2 == 0) { st2 = kStages - 1; ph2 ^= 1u; } else { --st2; }
+          mbar_wait_bounded(full_bar(st2), ph2, &never, kWaitLimitNs, kErrTimeoutDrain,
+                            &g_device_error_word);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (lw == 1) {
+    // ------------------------------ MMA issuer (pass 2) -----------------------
+    if (lane == 0) {
+      const uint64_t bdesc = umma_smem_desc(sbase + fz::kB, 256, 128, 0);
+      uint32_t stage = 0, phase = 0, acc = 0, accph = 0, j = 0;
+      bool ok = true;
+      if (p.b_tma && !mbar_wait_bounded(bfull_bar, 0, abort_flag, kWaitLimitNs, kErrTimeoutMma,
+                                        &g_device_error_word))
+        ok = false;
+      while (ok) {
+        const uint32_t sl = j % (uint32_t)fz::kQSlots, par = (j / (uint32_t)fz::kQSlots) & 1u;
+        if (!mbar_wait_bounded(qf_bar(sl), par, abort_flag, kWaitLimitNs, kErrTimeoutMma,
+                               &g_device_error_word))
+          break;
+        const int unit = qslot[sl];
+        mbar_arrive(qe_bar(sl));
+        ++j;
+        if (unit < 0) break;
+        const Unit t = unit_of(p, unit);
+        for (int a = 0; a < t.nacc && ok; ++a) {
+          if (!mbar_wait_bounded(acce0 + 8 * acc, accph ^ 1u, abort_flag, kWaitLimitNs,
+                                 kErrTimeoutMma, &g_device_error_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nh = (t.nsub - 2 * a) < 2 ? (t.nsub - 2 * a) : 2;
+          for (int h = 0; h < nh; ++h) {
+            if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, kWaitLimitNs,
+                                   kErrTimeoutMma, &g_device_error_word)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = hbase + fz::kA + stage * kStageBytes;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const uint64_t adesc = umma_smem_desc(a_base + g * 2048, kHalfBytes, 1024, 2);
+              tc_mma_f16_overwrite(tmem_base + acc * kAccN + h * kSubN + g * 16, adesc, bdesc,
+                                   kIdesc);
+            }
+            tc_commit(empty_bar(stage));
+            if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          tc_commit(accf0 + 8 * acc);
+          if (++acc == kAccStages) { acc = 0; accph ^= 1u; }
+        }
+      }
+      // All issued MMAs complete before TMEM is released.
+      tc_commit(drain_bar);
+      volatile uint32_t never = 0u;
+      mbar_wait_bounded(drain_bar, 0, &never, kWaitLimitNs, kErrTimeoutDrain,
+                        &g_device_error_word);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ----------------------------------
+    const int ew = lw - 2;
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int g = ew >> 2;            // k-block g of each stage: slices 2g, 2g + 1
+    const bool leader = (ew == 0 && lane == 0);
+    const bool cta_leader = leader && half == 0;
+    const uint32_t unit_bar = 1 + (uint32_t)half;   // named barrier of this half's epilogue
+    constexpr uint32_t kBothBar = 3;                // both halves' epilogues
+    const int tid = ew * 32 + lane;
+    uint32_t gen = 0;
+    if (cta_leader) gen = ld_acquire_gpu_u32(p.ws + kWsGen);   // before this block arrives
+
+    // Pass 1: NaN-propagating max of |A| (unsigned max of the bf16
+    // magnitude bits) over every stage this half's producer posts, 64 bytes
+    // per thread per 16 KiB stage, until the end marker.
+    uint32_t m2 = 0, st = 0, ph = 0;
+    while (true) {
+      if (!warp_wait(full1_bar(st), ph, abort_flag, kErrTimeoutEpilogue)) break;
+      const bool end = end_flag[st] != 0u;
+      if (!end) {
+        const uint32_t src = hbase + fz::kA + st * kStageBytes + (uint32_t)tid * 64u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 x = lds128(src + 16 * i);
+          m2 = __vmaxu2(m2, x.x & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, x.y & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, x.z & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, x.w & 0x7FFF7FFFu);
+        }
+      }
+      mbar_arrive(empty1_bar(st));
+      if (++st == kStages) { st = 0; ph ^= 1u; }
+      if (end) break;
+    }
+    const uint32_t mw = __reduce_max_sync(0xFFFFFFFFu, max(m2 & 0xFFFFu, m2 >> 16));
+    uint32_t* red = reinterpret_cast<uint32_t*>(smem + fz::kRed);
+    if (lane == 0) red[half * kEpiWarps + ew] = mw;
+    named_bar_sync(kBothBar, fz::kHalves * kEpiThreads);
+    if (cta_leader) {
+      // Grid barrier: each block folds its maximum into this launch's amax
+      // word (atomic max on the bits: amax >= 0, so integer order is value
+      // order and NaN wins) and arrives; the last to arrive clears the
+      // first-pass counter and the next launch's second-pass counter and
+      // amax word, and releases the grid.
+      uint32_t cta = 0;
+      for (int w = 0; w < fz::kHalves * kEpiWarps; ++w) cta = max(cta, red[w]);
+      const uint32_t par = gen & 1u;
+      atomicMax(p.ws + kWsAmax + par, cta << 16);      // this block's amax as fp32 bits
+      if (atom_add_acq_rel_gpu(p.ws + kWsArrive, 1u) == gridDim.x - 1) {
+        volatile uint32_t* ws = p.ws;
+        ws[kWsArrive] = 0u;
+        ws[kWsCnt1] = 0u;
+        ws[kWsCnt2 + (par ^ 1u)] = 0u;
+        ws[kWsAmax + (par ^ 1u)] = 0u;
+        st_release_gpu_u32(p.ws + kWsGen, gen + 1u);   // release the grid
+      } else {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu_u32(p.ws + kWsGen) == gen) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs || *abort_flag) {
+            *abort_flag = 1u;
+            atomicCAS(&g_device_error_word, 0u, (uint32_t)kErrTimeoutGridBarrier);
+            break;
+          }
+        }
+      }
+      const float local = __uint_as_float(ld_acquire_gpu_u32(p.ws + kWsAmax + par));
+      const float gm = launch_amax(p, local, abort_flag, kWaitLimitNs);
+      if (p.world <= 1 && blockIdx.x == 0 && p.amax_out != nullptr) *p.amax_out = gm;
+      *s_amax = gm;
+    }
+    named_bar_sync(kBothBar, fz::kHalves * kEpiThreads);
+    const float gamax = *s_amax;
+    if (half == 0) {
+      // reciprocal scale of every SFC code, and the Philox key schedule
+      const uint32_t code = (uint32_t)tid;
+      const float qs = e4m3_decode(code) * __fdiv_rn(1.0f, global_encode_scale(gamax));
+      const float rcp = FM ? rcp_approx_ftz(qs) : __fdiv_rn(1.0f, qs);
+      reinterpret_cast<float*>(smem + fz::kTab)[code] = fmin_nan(rcp, 3.402823466e38f);
+      if (SR && tid < 10) {
+        const uint64_t seed = p.rng != nullptr ? p.rng[0] : 0ull;
+        uint32_t* kt = reinterpret_cast<uint32_t*>(smem + fz::kKey);
+        kt[2 * tid] = (uint32_t)seed + (uint32_t)tid * 0x9E3779B9u;
+        kt[2 * tid + 1] = (uint32_t)(seed >> 32) + (uint32_t)tid * 0xBB67AE85u;
+      }
+    }
+    named_bar_sync(kBothBar, fz::kHalves * kEpiThreads);
+    const EpiThread e = epi_setup<SR>(p, q, g, lane, hbase + fz::kC, hbase + fz::kSfc, tmem_base,
+                                      sbase + fz::kTab, sbase + fz::kKey, gamax);
+
+    // Pass 2: units from this half's slots; epilogue warp 0 reads each slot
+    // and passes the unit on through shared memory.
+    auto take = [&](uint32_t j, bool ok_in) -> int {
+      const uint32_t sl = j % (uint32_t)fz::kQSlots, par = (j / (uint32_t)fz::kQSlots) & 1u;
+      int u = -1;
+      if (ok_in && warp_wait(qf_bar(sl), par, abort_flag, kErrTimeoutEpilogue)) {
+        u = qslot[sl];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qe_bar(sl));
+      }
+      return u;
+    };
+    bool ok = !*abort_flag;
+    if (ew == 0) {
+      const int u = take(0, ok);
+      if (lane == 0) next_unit[0] = u;
+    }
+    __syncwarp();
+    named_bar_sync(unit_bar, kEpiThreads);
+    int cur = next_unit[0];
+    uint32_t acc = 0, accph = 0, j = 1;
+    while (cur >= 0) {
+      const Unit t = unit_of(p, cur);
+      const uint32_t buf = j & 1u;
+      ok = epi_cast_unit<SR, FM>(p, t, e, buf, accf0, acce0, acc, accph, abort_flag);
+      fence_proxy_async_smem();
+      if (leader) bulk_wait_read_all();
+      if (ew == 0) {
+        const int u = take(j, ok);
+        if (lane == 0) next_unit[buf] = u;
+      }
+      __syncwarp();
+      named_bar_sync(unit_bar, kEpiThreads);
+      // (a warp whose wait gave up set the abort flag before the barrier)
+      if (!ok || *abort_flag) break;
+      epi_store_unit(p, t, &tmC, hbase + fz::kC + buf * kCTileBytes,
+                     hs + fz::kSfc + buf * kSfcTileBytes, ew, lane, leader);
+      cur = next_unit[buf];
+      ++j;
+    }
+    if (leader) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_all, fz::kHalves * kTmemCols);
   }
 }
 
@@ -1094,35 +1480,40 @@ int get_tensor_map(int kind, void* ptr, uint64_t d0, uint64_t d1, CUtensorMap* o
   return NVFP4_OK;
 }
 
+// The kernel of a (SR, FM, fused) combination with its launch shape.
+template <bool SR, bool FM, bool FUSED>
+struct KernelOf {
+  static constexpr auto fn = FUSED ? rht_fused_kernel<SR, FM> : rht_nvfp4_kernel<SR, FM>;
+  static constexpr int threads = FUSED ? fz::kThreadsF : kThreads;
+  static constexpr uint32_t smem = FUSED ? fz::kSmemBytes : kSmemBytes;
+};
+
 // Per-device, once: the kernel's shared-memory attributes; for the fused
 // kernel also the number of its blocks that fit on one SM (a cooperative
 // launch admits no more).
 template <bool SR, bool FM, bool FUSED>
 int prepare_kernel(int* per_sm) {
+  using K = KernelOf<SR, FM, FUSED>;
   static std::atomic<int> attr_set[64];
   static std::atomic<int> occupancy[64];
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
   if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM, FUSED>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kSmemBytes))
+    if (cudaError_t e = cudaFuncSetAttribute(K::fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)K::smem))
       return cuda_status(e);
-    // The largest shared-memory carveout, so that two CTAs fit on every SM.
-    if (cudaError_t e = cudaFuncSetAttribute(rht_nvfp4_kernel<SR, FM, FUSED>,
-                                             cudaFuncAttributePreferredSharedMemoryCarveout,
+    // The largest shared-memory carveout: two CTAs of the cast kernel, or
+    // the fused kernel's two pipelines, fit on every SM.
+    if (cudaError_t e = cudaFuncSetAttribute(K::fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                              (int)cudaSharedmemCarveoutMaxShared))
       return cuda_status(e);
     if (dev < 64) attr_set[dev].store(1, std::memory_order_release);
   }
   if constexpr (FUSED) {
-    // As many blocks per SM as the occupancy calculator reports for this
-    // kernel (one on current drivers, which count the TMEM-allocating kernel
-    // as one per SM, although two run side by side when launched normally).
     int n = dev < 64 ? occupancy[dev].load(std::memory_order_relaxed) : 0;
     if (n <= 0) {
-      if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-              &n, rht_nvfp4_kernel<SR, FM, FUSED>, kThreads, kSmemBytes))
+      if (cudaError_t e =
+              cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, K::fn, K::threads, K::smem))
         return cuda_status(e);
       if (n < 1) return cuda_status(cudaErrorCooperativeLaunchTooLarge);
       if (dev < 64) occupancy[dev].store(n, std::memory_order_relaxed);
@@ -1137,10 +1528,11 @@ int prepare_kernel(int* per_sm) {
 template <bool SR, bool FM, bool FUSED>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tb,
                   const Params& p, int grid, cudaStream_t stream) {
+  using K = KernelOf<SR, FM, FUSED>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.blockDim = dim3(K::threads);
+  cfg.dynamicSmemBytes = K::smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   if constexpr (!FUSED) {
@@ -1156,8 +1548,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMa
   }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaError_t e = cudaLaunchKernelEx(&cfg, rht_nvfp4_kernel<SR, FM, FUSED>, ta, tc, tb, p))
-    return cuda_status(e);
+  if (cudaError_t e = cudaLaunchKernelEx(&cfg, K::fn, ta, tc, tb, p)) return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
 
@@ -1179,13 +1570,12 @@ KernelEntry kernel_entry(bool sr, bool fm, bool fused) {
   return table[(fused ? 4 : 0) + (sr ? 2 : 0) + (fm ? 1 : 0)];
 }
 
-// How the fused kernel's grid-barrier workspace is handled.
+// How the fused kernel's workspace is handled.
 enum class WsMode {
-  kCaller,      // caller-owned workspace; a grid above its capacity is clamped
-  kStaticClear  // the library's static scratch: a grid above its capacity is
-                // refused, and its arrival counter is cleared (a 4-byte
-                // memset on the stream) right before the launch, after every
-                // check has passed
+  kCaller,      // caller-owned workspace, zeroed by the caller before first use
+  kStaticClear  // the library's static scratch: its counters and amax words are
+                // cleared (a 24-byte memset on the stream) right before the
+                // launch, after every check has passed
 };
 
 int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
@@ -1198,7 +1588,7 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
   if (n_total <= 0) n_total = n;
-  if (n_offset < 0 || n_offset + n > n_total) return NVFP4_ERR_INVALID_SHAPE;
+  if (n_offset < 0 || (int64_t)n_offset + n > (int64_t)n_total) return NVFP4_ERR_INVALID_SHAPE;
   const int kt = n_total < k_tile_size ? n_total : k_tile_size;
   const uint32_t ktm = (uint32_t)(kt / 64);
   if (n_offset % (int)(ktm * 64) != 0) return NVFP4_ERR_INVALID_SHAPE;
@@ -1206,6 +1596,11 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   if (!A || !B || !C || !SFC || (!global_amax && !fused)) return NVFP4_ERR_INVALID_ARGUMENT;
   if (fused && (uintptr_t)fused_ws % 4) return NVFP4_ERR_MISALIGNED;
   if ((uintptr_t)A % 16 || (uintptr_t)C % 16 || (uintptr_t)B % 2) return NVFP4_ERR_MISALIGNED;
+  // Work units are counted in 32-bit integers (the grid of the balanced
+  // schedule, the fused kernel's unit counters): at most 2^31 - 1 of them.
+  const int64_t units64 = (int64_t)(m / kBM) * (((int64_t)n + kUnitN - 1) / kUnitN);
+  if (units64 > (int64_t)kMaxUnits)
+    return ws_mode == WsMode::kStaticClear ? NVFP4_ERR_SCRATCH_CAPACITY : NVFP4_ERR_INVALID_SHAPE;
   int sms = 0;
   if (int e = device_sm_count(&sms)) return e;
 
@@ -1218,7 +1613,7 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   p.m = m;
   p.n = n;
   p.tiles_m = m / kBM;
-  p.units = p.tiles_m * ((n + kUnitN - 1) / kUnitN);
+  p.units = (int)units64;
   p.n_offset = n_offset;
   p.ktm = ktm;
   p.div_ktm = make_fast_div(ktm);
@@ -1242,12 +1637,17 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
 
   int grid = sms;
   if (sm_count > 0 && (int)sm_count < grid) grid = (int)sm_count;
-  grid *= 2;   // two CTAs per SM
-  if (p.units < grid) grid = p.units;
-  if (!fused && grid == 2 * sms) {
-    // All SMs in use: one CTA per unit, balanced by cluster launch control.
-    p.dynamic = 1;
-    grid = p.units;
+  if (fused) {
+    // one CTA (two pipelines) per SM, no more than the units can keep busy
+    if ((p.units + 1) / 2 < grid) grid = (p.units + 1) / 2;
+  } else {
+    grid *= 2;   // two CTAs per SM
+    if (p.units < grid) grid = p.units;
+    if (grid == 2 * sms) {
+      // All SMs in use: one CTA per unit, balanced by cluster launch control.
+      p.dynamic = 1;
+      grid = p.units;
+    }
   }
 
   const KernelEntry k = kernel_entry(sr, fm, fused);
@@ -1255,12 +1655,8 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
   if (int e = k.prepare(&per_sm)) return e;
   if (fused) {
     if (grid > per_sm * sms) grid = per_sm * sms;   // all blocks resident
-    if (grid > kMaxFusedCtas) {
-      if (ws_mode == WsMode::kStaticClear) return NVFP4_ERR_SCRATCH_CAPACITY;
-      grid = kMaxFusedCtas;
-    }
     if (ws_mode == WsMode::kStaticClear) {
-      if (cudaError_t e = cudaMemsetAsync(fused_ws, 0, sizeof(uint32_t), stream))
+      if (cudaError_t e = cudaMemsetAsync(fused_ws, 0, kWsClearBytes, stream))
         return cuda_status(e);
     }
   }
@@ -1321,7 +1717,8 @@ NVFP4_API const char* nvfp4_status_string(int status) {
     case NVFP4_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs compute capability 10.0)";
     case NVFP4_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out";
     case NVFP4_ERR_SCRATCH_CAPACITY:
-      return "launch needs more blocks than the static scratch of the no-allocation entry holds";
+      return "problem has more work units (128 x 256 tiles) than the no-allocation entry's "
+             "built-in scratch counts (2^31 - 1)";
     default: return "unknown status";
   }
 }
@@ -1472,9 +1869,10 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
 
 // ---------------------------------------------------------------------------
 // Fused amax + cast without any allocation by the caller or the library.
-// The grid-barrier workspace lives in this static device array (kFusedWsWords
-// 32-bit words, 4112 bytes, on every GPU that loads the library, until the
-// process exits).  Host code must not hand the array's name to a kernel:
+// The workspace (grid-barrier count, unit counters, amax words: kFusedWsWords
+// 32-bit words, 32 bytes whatever the problem size) lives in this static
+// device array, on every GPU that loads the library, until the process
+// exits.  Host code must not hand the array's name to a kernel:
 // there it only stands for the symbol, so its device address is looked up
 // once per device with cudaGetSymbolAddress.
 // ---------------------------------------------------------------------------
@@ -1512,12 +1910,15 @@ NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, cons
   if (m == 0 || n == 0) return NVFP4_OK;
   if (m % nvfp4::rht::kBM != 0 || n % 64 != 0 || k_tile_size < 64) return NVFP4_ERR_INVALID_SHAPE;
   if (!A || !B || !C || !SFC) return NVFP4_ERR_INVALID_ARGUMENT;
+  if ((int64_t)(m / nvfp4::rht::kBM) * (((int64_t)n + nvfp4::rht::kUnitN - 1) / nvfp4::rht::kUnitN) >
+      (int64_t)nvfp4::rht::kMaxUnits)
+    return NVFP4_ERR_SCRATCH_CAPACITY;
   uint32_t* scratch = nullptr;
   if (int e = fused_scratch_address(&scratch)) return e;
-  // rht_launch checks shapes, pointers and the grid against the scratch's
-  // capacity first; only a call that passes every check enqueues anything:
-  // a 4-byte memset of the arrival count (a launch that gave up part-way may
-  // have left it nonzero; the other words need no clearing), then the kernel.
+  // rht_launch checks shapes, pointers and the unit count against the
+  // scratch's 32-bit counters first; only a call that passes every check
+  // enqueues anything: a 24-byte memset of the counters and amax words (a
+  // launch that gave up part-way may have left them nonzero), then the kernel.
   return rht_launch(m, n, A, B, C, SFC, nullptr, rng_state, sm_count, (cudaStream_t)stream,
                     k_tile_size, stochastic_rounding != 0, use_fast_math != 0, 0, n, nullptr, 0,
                     1, 0, amax_out, scratch, nvfp4::rht::WsMode::kStaticClear);

@@ -39,8 +39,8 @@ enum nvfp4_status {
   NVFP4_ERR_CUDA = 4,             /* a CUDA runtime call failed (see nvfp4_last_cuda_error) */
   NVFP4_ERR_UNSUPPORTED_DEVICE = 5, /* not a compute capability 10.0 device */
   NVFP4_ERR_DEVICE_TIMEOUT = 6,   /* a kernel's bounded wait gave up (nvfp4_device_error) */
-  NVFP4_ERR_SCRATCH_CAPACITY = 7  /* more blocks than nvfp4_quantize_rht_fused_noalloc's
-                                     built-in scratch holds (1024) */
+  NVFP4_ERR_SCRATCH_CAPACITY = 7  /* more work units than nvfp4_quantize_rht_fused_noalloc's
+                                     built-in scratch counts (2^31 - 1) */
 };
 
 /* Human-readable text for a status code. */
@@ -106,15 +106,17 @@ NVFP4_API int nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange(
     int k_tile_size, int stochastic_rounding, int use_fast_math, int n_offset, int n_total,
     nvfp4_exchange* ex);
 
-/* Global amax and cast in ONE kernel (no separate pre-pass): a first pass
- * streams A through the kernel's TMA ring to take the NaN-propagating max of
- * |A|, the blocks meet at a grid barrier (cooperative launch, one block per
- * SM), and the cast then walks its tiles in reverse so that the tiles read
- * last are re-read from L2.  Writes the amax to *amax_out (device float, may
- * be NULL).  Results equal nvfp4_amax_bf16 followed by
- * nvfp4_rht_gemm_ntt_w_sfc.  `workspace` is nvfp4_fused_workspace_bytes()
- * bytes of device memory, zeroed once before first use, never used by two
- * launches at the same time; each launch leaves it ready for the next.
+/* Global amax and cast in ONE kernel (no separate pre-pass).  One block per
+ * SM (cooperative launch) runs two independent pipelines; in a first pass
+ * they stream A through their TMA rings and take the NaN-propagating max of
+ * |A|, the blocks meet at a grid barrier, and the cast then takes the units
+ * in descending order, so that the tiles the first pass read last are
+ * re-read from L2.  Writes the amax to *amax_out (device float, may be NULL).
+ * Results equal nvfp4_amax_bf16 followed by nvfp4_rht_gemm_ntt_w_sfc.
+ * `workspace` is nvfp4_fused_workspace_bytes() (32) bytes of device memory,
+ * zeroed once before first use, never used by two launches at the same time;
+ * each completed launch leaves it ready for the next (zero it again after a
+ * launch that reported NVFP4_ERR_DEVICE_TIMEOUT).
  * No reference counterpart: the reference takes the amax as an input and has
  * no amax kernel; this is the fused form its callers would otherwise need. */
 NVFP4_API size_t nvfp4_fused_workspace_bytes(void);
@@ -128,24 +130,23 @@ NVFP4_API int nvfp4_quantize_rht_fused(int m, int n, const void* A, const void* 
  * memory through their own pool and do not let a library call cudaMalloc
  * (it can synchronize the device and bypasses the pool), so they cannot
  * provide nvfp4_quantize_rht_fused's workspace.  This entry point takes the
- * same inputs and outputs but keeps the grid-barrier scratch in a 4112-byte
- * array built into the library: every GPU that loads the library holds it
- * until the process exits, and no call allocates anything.
- *   - Limit: a launch may use at most 1024 blocks.  The grid is the
- *     cooperative launch's co-resident block count (one per SM on a B200,
- *     148); a grid above 1024 is refused with NVFP4_ERR_SCRATCH_CAPACITY
- *     before anything is enqueued.
+ * same inputs and outputs but keeps that workspace in a 32-byte array built
+ * into the library: every GPU that loads the library holds it until the
+ * process exits, and no call allocates anything.
+ *   - Limit: the array's 32-bit counters hand out at most 2^31 - 1 work units
+ *     (128 x 256 tiles of A) per call; a larger problem is refused with
+ *     NVFP4_ERR_SCRATCH_CAPACITY before anything is enqueued.
  *   - A refused call (bad shape, pointer, alignment or capacity) enqueues
  *     nothing on `stream`.
- *   - The looked-up address is kept per device; it is not valid after a
- *     cudaDeviceReset of that device.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     The looked-up address is kept per device; it is not valid after a
+ *     cudaDeviceReset of that device.
  *   - All calls share the one array: calls that may overlap on the GPU (other
  *     streams, other host threads) race and must be serialized by the caller.
- *     Each call clears the arrival counter it needs at zero (a 4-byte
- *     cudaMemsetAsync on `stream`); the array otherwise keeps the last call's
- *     contents. */
+ *     Each call clears the counters and amax words it needs at zero (a
+ *     24-byte cudaMemsetAsync on `stream`); the array otherwise keeps the
+ *     last call's contents. */
 NVFP4_API int nvfp4_quantize_rht_fused_noalloc(int m, int n, const void* A, const void* B,
                                                void* C, void* SFC, float* amax_out,
                                                const size_t* rng_state, uint32_t sm_count,

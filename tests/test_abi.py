@@ -123,3 +123,18 @@ def test_ttt_wrapper_swaps_m_and_n(nvlib):
                                   0) == 2     # passes the shape check, then refuses NULL A
     assert lib.nvfp4_rht_gemm_ttt(0, 128, None, None, None, None, None, None, 0, None, 2048, 0,
                                   0) == 0
+
+
+def test_noalloc_rejects_more_units_than_its_scratch_counts(nvlib):
+    """nvfp4_quantize_rht_fused_noalloc's built-in scratch counts work units
+    (128 x 256 tiles) in 32 bits: a problem with more than 2^31 - 1 of them is
+    refused with NVFP4_ERR_SCRATCH_CAPACITY by the argument checks, before
+    any CUDA call (so this runs without a GPU; the pointers are placeholders
+    that are never used)."""
+    from fp4_sm120a_b200 import _native
+    lib = _native.load()
+    m, n = 2**31 - 128, 2**31 - 64          # 16777215 x 8388608 units
+    rc = lib.nvfp4_quantize_rht_fused_noalloc(m, n, 256, 256, 256, 256, None, None, 0, None,
+                                              2048, 1, 0)
+    assert rc == 7, lib.nvfp4_status_string(rc)
+    assert b"scratch" in lib.nvfp4_status_string(7)

@@ -48,19 +48,6 @@ def test_noalloc_matches_workspace_entry_twice():
             assert torch.equal(C, C0)
 
 
-def test_noalloc_rejects_more_blocks_than_its_scratch_holds():
-    from fp4_sm120a_b200 import _native
-    lib = _native.load()
-    if torch.cuda.get_device_properties(0).multi_processor_count <= 1024:
-        # sm_count above the device's SM count is capped to it, so on a B200
-        # (148 SMs) the limit cannot be exceeded; check the documented code.
-        assert b"scratch" in lib.nvfp4_status_string(7)
-    else:
-        rc = lib.nvfp4_quantize_rht_fused_noalloc(128, 64, 16, 16, 16, 16, None, None, 2048,
-                                                  None, 2048, 0, 0)
-        assert rc == 7
-
-
 def test_noalloc_refused_call_enqueues_nothing():
     """A call refused for a misaligned A returns NVFP4_ERR_MISALIGNED and puts
     nothing on the stream: captured on a side stream, it leaves an empty graph."""
