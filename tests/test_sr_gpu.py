@@ -197,3 +197,27 @@ def test_rowwise_quantize_cfg3_full_vs_oracle(nvlib, orc):
     gs, gc = host(S, np.uint8), host(C, np.uint8)
     assert (gs == ws).all(), f"SFC mismatches: {(gs != ws).sum()}"
     assert (gc == wc).all(), f"FP4 byte mismatches: {(gc != wc).sum()}"
+
+
+@pytest.mark.parametrize("n", [(8 << 20) // 2, (1 << 27) + 5, 65536 * 14336])
+def test_amax_large_tensors_vs_torch(nvlib, n):
+    """Tensors of 8 MB and more take the bulk-copy amax kernel (32 KiB
+    chunks, ragged last chunk, < 8 trailing values): its amax equals torch's
+    max of |x| bit for bit, and a NaN anywhere (here in the ragged tail region
+    and in the middle) propagates."""
+    g = torch.Generator(device="cuda").manual_seed(n % 1000)
+    x = torch.randn(n, device="cuda", generator=g)
+    x[torch.rand(n, device="cuda", generator=g) < 0.001] *= 50.0
+    xb = x.to(torch.bfloat16)
+    del x
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    nvlib.amax_bf16(xb, n, out)
+    want = xb.float().abs().max().view(1)
+    assert torch.equal(out.view(torch.int32), want.view(torch.int32)), (out, want)
+    for pos in (n - 1, n // 2):
+        saved = xb[pos].clone()
+        xb[pos] = float("nan")
+        nvlib.amax_bf16(xb, n, out)
+        assert torch.isnan(out).all(), pos
+        xb[pos] = saved
+    assert nvlib.device_error() == 0
