@@ -24,7 +24,6 @@ enum DeviceError : uint32_t {
   kErrTimeoutDrain = 4,
   kErrTimeoutExchange = 5,
   kErrTimeoutGridBarrier = 6,
-  kErrTimeoutAmax = 7,
 };
 
 // ---------------------------------------------------------------------------
@@ -254,16 +253,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
       "[%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(tmap), "r"(bar), "r"(x), "r"(y)
-      : "memory");
-}
-// Bulk (non-tensor) copy of `bytes` from global to shared memory, completing
-// on an mbarrier; both addresses 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
 // 2-D TMA tile store from shared memory (bulk-group completion).

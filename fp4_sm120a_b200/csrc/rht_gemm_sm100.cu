@@ -1394,122 +1394,6 @@ __global__ void __launch_bounds__(fz::kThreadsF, 1)
 
 
 // ---------------------------------------------------------------------------
-// Global amax pre-pass through bulk copies: k_amax_bulk
-//
-// One CTA per SM streams 32 KiB chunks of A (chunk c = blockIdx.x + k *
-// gridDim.x) into a 6-stage shared-memory ring with cp.async.bulk; its 8 warps
-// take the NaN-propagating max of the bf16 magnitude bits from shared memory.
-// The copy engine keeps ~192 KiB per SM in flight with one issuing thread,
-// which reads HBM faster than per-thread 16-byte loads (7.2-7.4 TB/s read-only
-// against ~6.5).
-// ---------------------------------------------------------------------------
-namespace amx {
-constexpr int kThreadsA = 256;
-constexpr int kStagesA = 6;
-constexpr uint32_t kChunk = 32768;
-constexpr uint32_t kOffBarA = kStagesA * kChunk;
-constexpr uint32_t kSmemA = kOffBarA + 16 * kStagesA + 16 + 128;   // + alignment slack
-}  // namespace amx
-
-__global__ void __launch_bounds__(amx::kThreadsA, 1)
-    k_amax_bulk(const uint8_t* __restrict__ x, size_t nbytes, const uint16_t* __restrict__ tail,
-                int ntail, uint32_t* __restrict__ out_bits) {
-  // The next kernel (the cast) may launch now; it waits for this one to
-  // complete before it reads the amax.
-  asm volatile("griddepcontrol.launch_dependents;");
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
-  const uint32_t sbase = smem_addr(smem);
-  const uint32_t bar0 = sbase + amx::kOffBarA;
-  auto full_bar = [&](uint32_t s) { return bar0 + 8 * s; };
-  auto empty_bar = [&](uint32_t s) { return bar0 + 8 * (amx::kStagesA + s); };
-  volatile uint32_t* abort_flag =
-      reinterpret_cast<volatile uint32_t*>(smem + amx::kOffBarA + 16 * amx::kStagesA);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const size_t nchunks = (nbytes + amx::kChunk - 1) / amx::kChunk;
-  auto chunk_bytes = [&](size_t c) -> uint32_t {
-    const size_t rest = nbytes - c * amx::kChunk;
-    return rest < amx::kChunk ? (uint32_t)rest : amx::kChunk;
-  };
-  uint32_t issued = 0;
-  if (tid == 0) {
-    for (uint32_t s = 0; s < (uint32_t)amx::kStagesA; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), amx::kThreadsA / 32);   // one arrival per warp
-    }
-    *abort_flag = 0u;
-    fence_barrier_init();
-    for (uint32_t s = 0; s < (uint32_t)amx::kStagesA; ++s) {
-      const size_t c = blockIdx.x + (size_t)s * gridDim.x;
-      if (c >= nchunks) break;
-      mbar_arrive_expect_tx(full_bar(s), chunk_bytes(c));
-      bulk_load(sbase + s * amx::kChunk, x + c * amx::kChunk, chunk_bytes(c), full_bar(s));
-      ++issued;
-    }
-  }
-  __syncthreads();
-  uint32_t m2 = 0;
-  bool ok = true;
-  uint32_t k = 0;
-  for (;; ++k) {
-    const size_t c = blockIdx.x + (size_t)k * gridDim.x;
-    if (c >= nchunks) break;
-    const uint32_t s = k % amx::kStagesA, ph = (k / amx::kStagesA) & 1u;
-    if (!warp_wait(full_bar(s), ph, abort_flag, kErrTimeoutAmax)) {
-      ok = false;
-      break;
-    }
-    const uint32_t bytes = chunk_bytes(c);
-#pragma unroll
-    for (int i = 0; i < (int)(amx::kChunk / (16 * amx::kThreadsA)); ++i) {
-      const uint32_t off = (uint32_t)(i * amx::kThreadsA + tid) * 16u;
-      if (off < bytes) {
-        const uint4 v = lds128(sbase + s * amx::kChunk + off);
-        m2 = __vmaxu2(m2, v.x & 0x7FFF7FFFu);
-        m2 = __vmaxu2(m2, v.y & 0x7FFF7FFFu);
-        m2 = __vmaxu2(m2, v.z & 0x7FFF7FFFu);
-        m2 = __vmaxu2(m2, v.w & 0x7FFF7FFFu);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar(s));
-    if (tid == 0) {
-      // refill this stage with the chunk kStagesA ahead once every warp is done
-      const size_t cn = blockIdx.x + (size_t)(k + amx::kStagesA) * gridDim.x;
-      if (cn < nchunks) {
-        if (!mbar_wait_bounded(empty_bar(s), ph, abort_flag, kWaitLimitNs, kErrTimeoutAmax,
-                               &g_device_error_word)) {
-          ok = false;
-        } else {
-          mbar_arrive_expect_tx(full_bar(s), chunk_bytes(cn));
-          bulk_load(sbase + s * amx::kChunk, x + cn * amx::kChunk, chunk_bytes(cn), full_bar(s));
-          ++issued;
-        }
-      }
-    }
-  }
-  if (tid == 0 && !ok) {
-    // Let the copies already in flight land before the CTA exits.
-    volatile uint32_t never = 0u;
-    for (uint32_t j = k; j < issued; ++j)
-      mbar_wait_bounded(full_bar(j % amx::kStagesA), (j / amx::kStagesA) & 1u, &never,
-                        kWaitLimitNs, kErrTimeoutDrain, &g_device_error_word);
-  }
-  if (blockIdx.x == 0 && tid < ntail) m2 = __vmaxu2(m2, (uint32_t)(tail[tid] & 0x7FFFu));
-  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
-  m = __reduce_max_sync(0xFFFFFFFFu, m);
-  __shared__ uint32_t warp_max[amx::kThreadsA / 32];
-  if (lane == 0) warp_max[warp] = m;
-  __syncthreads();
-  if (warp == 0) {
-    m = lane < amx::kThreadsA / 32 ? warp_max[lane] : 0u;
-    m = __reduce_max_sync(0xFFFFFFFFu, m);
-    if (lane == 0 && m != 0u) atomicMax(out_bits, m << 16);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -1781,28 +1665,6 @@ int rht_launch(int m, int n, const void* A, const void* B, void* C, void* SFC,
 }
 
 }  // namespace rht
-
-int amax_bulk_launch(const void* x, size_t nbytes, const uint16_t* tail, int ntail,
-                     uint32_t* out_bits, cudaStream_t stream) {
-  static std::atomic<int> attr_set[64];
-  int dev = 0;
-  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e);
-  if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaError_t e = cudaFuncSetAttribute(rht::k_amax_bulk,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)rht::amx::kSmemA))
-      return cuda_status(e);
-    if (dev < 64) attr_set[dev].store(1, std::memory_order_release);
-  }
-  int sms = 0;
-  if (int e = device_sm_count(&sms)) return e;
-  const size_t nchunks = (nbytes + rht::amx::kChunk - 1) / rht::amx::kChunk;
-  int grid = sms;
-  if (nchunks < (size_t)grid) grid = (int)(nchunks > 0 ? nchunks : 1);
-  rht::k_amax_bulk<<<grid, rht::amx::kThreadsA, rht::amx::kSmemA, stream>>>(
-      reinterpret_cast<const uint8_t*>(x), nbytes, tail, ntail, out_bits);
-  return cuda_status(cudaGetLastError());
-}
 
 // ---------------------------------------------------------------------------
 // Shared host helpers

@@ -346,12 +346,6 @@ NVFP4_API int nvfp4_amax_bf16(const void* x, size_t n, float* out, nvfp4_stream_
   if (int e = device_sm_count(&sms)) return e;
   const size_t nvec = n / 8;
   const int ntail = (int)(n % 8);
-  if (nvec * 16 >= ((size_t)8 << 20)) {
-    // large tensors: the bulk-copy kernel (one issuing thread per SM keeps
-    // the HBM read queue full)
-    return amax_bulk_launch(x, nvec * 16, reinterpret_cast<const uint16_t*>(x) + nvec * 8, ntail,
-                            reinterpret_cast<uint32_t*>(out), st);
-  }
   size_t blocks = (nvec + 511) / 512;
   if (blocks > (size_t)sms * 4) blocks = (size_t)sms * 4;
   if (blocks == 0) blocks = 1;

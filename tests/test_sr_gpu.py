@@ -201,10 +201,9 @@ def test_rowwise_quantize_cfg3_full_vs_oracle(nvlib, orc):
 
 @pytest.mark.parametrize("n", [(8 << 20) // 2, (1 << 27) + 5, 65536 * 14336])
 def test_amax_large_tensors_vs_torch(nvlib, n):
-    """Tensors of 8 MB and more take the bulk-copy amax kernel (32 KiB
-    chunks, ragged last chunk, < 8 trailing values): its amax equals torch's
-    max of |x| bit for bit, and a NaN anywhere (here in the ragged tail region
-    and in the middle) propagates."""
+    """Large tensors (up to the full cfg5 activation, and a length with < 8
+    trailing values): the amax equals torch's max of |x| bit for bit, and a
+    NaN anywhere (here in the trailing values and in the middle) propagates."""
     g = torch.Generator(device="cuda").manual_seed(n % 1000)
     x = torch.randn(n, device="cuda", generator=g)
     x[torch.rand(n, device="cuda", generator=g) < 0.001] *= 50.0
