@@ -11,6 +11,9 @@ each rank runs
        amax over NVLink peer memory before its first quantization
        (nvfp4_rht_gemm_ntt_w_sfc_sharded_exchange; --exchange nccl uses an
        NCCL int32-MAX all-reduce of the scalar between the two kernels instead).
+Per-rank problems of >= 14336 x 32768 elements (N <= 2) run the step as the
+fused single kernel instead (nvfp4_quantize_rht_fused[_sharded_exchange]:
+amax pass, grid barrier, cast), which is faster there (--path chooses).
 `value` is GB/s in the reference's byte convention for the cast
 (2.5625 B per element: 2 read + 0.5 FP4 + 0.0625 SFC, rht_gemm/test_compare.cu:256)
 over all ranks' elements divided by the max-over-ranks step time; the amax
@@ -335,7 +338,8 @@ def bench_reference(args):
         "scaling": "strong",
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(args.gpus, args.exchange),
+        "config": workload_config(args.gpus, args.exchange,
+                                  step_path(args, COLS, ROWS // args.gpus)),
         "elem_per_s": base["elem_per_s"],
         "sr_software": sr_software_baseline(),
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -347,23 +351,45 @@ def bench_reference(args):
     return 0
 
 
-def workload_config(n, exchange="peer"):
+def workload_config(n, exchange="peer", path="two"):
     ex = "none" if n == 1 else exchange
-    how = {"none": "amax pre-pass + RHT GEMM + NVFP4 cast",
-           "peer": "amax pre-pass + RHT GEMM + NVFP4 cast with the ranks' amax combined "
-                   "inside the cast kernel over NVLink peer memory",
-           "nccl": "amax pre-pass + NCCL int32-MAX all-reduce of the amax + RHT GEMM + "
-                   "NVFP4 cast"}[ex]
+    if path == "fused":
+        how = {"none": "global amax and RHT GEMM + NVFP4 cast in one kernel "
+                       "(nvfp4_quantize_rht_fused)",
+               "peer": "global amax and RHT GEMM + NVFP4 cast in one kernel, the ranks' amax "
+                       "combined inside it over NVLink peer memory",
+               "nccl": "global amax and RHT GEMM + NVFP4 cast in one kernel"}[ex]
+    else:
+        how = {"none": "amax pre-pass + RHT GEMM + NVFP4 cast",
+               "peer": "amax pre-pass + RHT GEMM + NVFP4 cast with the ranks' amax combined "
+                       "inside the cast kernel over NVLink peer memory",
+               "nccl": "amax pre-pass + NCCL int32-MAX all-reduce of the amax + RHT GEMM + "
+                       "NVFP4 cast"}[ex]
     return {"workload": "BASELINE cfg5: X 65536x14336 bf16 N(0,1)+0.1% x50 outliers, "
                         f"row-sharded (API m=14336, n=65536/N per rank), {how}, "
                         "stochastic rounding",
             "m": COLS, "n_total": ROWS, "n_per_rank": ROWS // n, "k_tile_size": 2048,
             "stochastic_rounding": True, "parallelism": f"row-shard x{n}",
-            "amax_exchange": ex,
+            "amax_exchange": ex, "path": path,
             "l2": "inputs larger than L2 (per-rank shard >= 235 MB > 126 MB)"}
 
 
-def check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank):
+# Per-rank problems of at least this many elements run the step as the fused
+# single kernel (--path auto): there its second pass re-reads part of A from
+# L2 and it saves a launch; below it the amax kernel + cast kernel are faster
+# (measured on one B200, m = 14336: fused 638-644 vs 659-664 us at n = 65536,
+# 331 vs 336 us at n = 32768, 177 vs 174 us at n = 16384, 101 vs 96 us at
+# n = 8192).
+FUSED_MIN_ELEMS = 14336 * 32768
+
+
+def step_path(args, m, n_per_rank):
+    if args.path != "auto":
+        return args.path
+    return "fused" if m * n_per_rank >= FUSED_MIN_ELEMS else "two"
+
+
+def check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank, fused=False):
     """Bit-for-bit check of the step's outputs (C, S and the amax of the
     last step) against independent paths.  N = 1: the fused single-kernel
     quantizer.  N > 1: (a) on every rank, the NCCL path -- amax kernel,
@@ -375,16 +401,23 @@ def check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank):
     C2, S2 = torch.empty_like(C), torch.empty_like(S)
     am2 = torch.empty(1, dtype=torch.float32, device="cuda")
     if ws == 1:
-        wsp = nv.fused_workspace()
-        nv.quantize_rht_fused(m, n, A, B, C2, S2, am2, rng_state, wsp, 0, None, 2048,
-                              stochastic_rounding=True)
+        if fused:
+            # the step ran the fused kernel: check it against amax + cast
+            nv.amax_bf16(A, m * n, am2)
+            nv.rht_gemm_ntt_w_sfc(m, n, A, B, C2, S2, am2, rng_state, 0, None, 2048,
+                                  stochastic_rounding=True)
+            vs = "amax kernel + cast kernel (nvfp4_amax_bf16, nvfp4_rht_gemm_ntt_w_sfc), same input"
+        else:
+            wsp = nv.fused_workspace()
+            nv.quantize_rht_fused(m, n, A, B, C2, S2, am2, rng_state, wsp, 0, None, 2048,
+                                  stochastic_rounding=True)
+            vs = "fused single-kernel quantizer (nvfp4_quantize_rht_fused), same input"
         torch.cuda.synchronize()
         cnt = torch.tensor([int((C2 != C).sum()), int((S2 != S).sum()),
                             int(not torch.equal(am2.view(torch.int32), amax.view(torch.int32)))],
                            dtype=torch.int64)
         return {"checked": True, "fp4_mismatch": int(cnt[0]), "sfc_mismatch": int(cnt[1]),
-                "amax_mismatch": int(cnt[2]),
-                "vs": "fused single-kernel quantizer (nvfp4_quantize_rht_fused), same input"}
+                "amax_mismatch": int(cnt[2]), "vs": vs}
     # (a) this rank's shard through the NCCL exchange path
     nv.amax_bf16(A, m * n, am2)
     combine_amax(am2)
@@ -514,8 +547,9 @@ def bench_ours(args):
     m = COLS
     n_total = ROWS
     rng_state = torch.tensor([SEED, 0], dtype=torch.int64, device="cuda")
+    fused = step_path(args, m, n_total // ws) == "fused"
     qz = ShardedRhtQuantizer(m, n_total, k_tile_size=2048, stochastic_rounding=True,
-                             rng_state=rng_state, exchange=args.exchange)
+                             rng_state=rng_state, exchange=args.exchange, fused=fused)
     n = qz.n
     A = make_shard(torch, rank, n)
     B = nv.hadamard16(torch.where(torch.arange(16) % 3 == 0, -1.0, 1.0), device="cuda")
@@ -525,6 +559,14 @@ def bench_ours(args):
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
+        if fused:
+            # one kernel: amax pass, (peer exchange,) cast
+            if ev is not None:
+                ev[0].record(stream)
+            qz(A, B, C, S, amax, stream)
+            if ev is not None:
+                ev[1].record(stream)
+            return
         # amax pre-pass -> exchange of the scalar -> RHT + NVFP4 cast.  With the
         # peer exchange the cast kernel itself combines the ranks' amax.
         nv.amax_bf16(A, m * n, amax, stream)
@@ -608,7 +650,7 @@ def bench_ours(args):
     if ws > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms_total, rht_ms, sus_ms = tt.tolist()
-    parity = check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank)
+    parity = check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank, fused)
     ms_step = ms_total / args.steps
     elems_total = m * n_total
     value = elems_total * BYTES_PER_ELEM / (ms_step * 1e-3) / 1e9
@@ -645,13 +687,17 @@ def bench_ours(args):
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        rht_bytes = m * n * BYTES_PER_ELEM + RHT_FIXED_BYTES
+        # the timed kernel: the cast (2.5625 B/elem), or the fused kernel, which
+        # also reads A for the amax (4.5625 B/elem)
+        kbpe = BYTES_PER_ELEM + (2.0 if fused else 0.0)
+        rht_bytes = m * n * kbpe + RHT_FIXED_BYTES
         achieved = rht_bytes / (rht_ms * 1e-3) / 1e9
         traffic = None
         tp = ROOT / "profiles" / "rht_nvfp4_traffic.txt"
         if tp.exists():
             for line in tp.read_text().splitlines():
-                if line.startswith("dram_bytes_per_element"):
+                key = "fused_dram_bytes_per_element" if fused else "dram_bytes_per_element"
+                if line.startswith(key + " "):
                     traffic = round(float(line.split("=")[1]) * m * n)
         clocks = sampler.summary() if sampler else {}
         line = {
@@ -667,19 +713,23 @@ def bench_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 with 0.1% x50 outliers; BASELINE cfg5 shape)",
-            "config": workload_config(ws, args.exchange),
+            "config": workload_config(ws, args.exchange, "fused" if fused else "two"),
             "elem_per_s": elems_total / (ms_step * 1e-3),
             "frac_of_8TBs": round(value / NOMINAL_HBM_GBS, 4),
             "step_hbm_gbs": round(elems_total * (BYTES_PER_ELEM + 2.0) / (ms_step * 1e-3) / 1e9,
                                   2),
-            "roofline": {"bound": "hbm", "kernel": "rht_nvfp4_kernel<SR=1,FM=0>",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("rht_fused_kernel<SR=1,FM=0>" if fused
+                                    else "rht_nvfp4_kernel<SR=1,FM=0>"),
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_launch": rht_bytes,
                          "avg_launch_ms": round(rht_ms, 5),
-                         "launch_timing": "CUDA events around each cast over a second pass "
-                                          "of the K steps, right after the timed region"},
+                         "launch_timing": "CUDA events around each "
+                                          + ("fused launch" if fused else "cast")
+                                          + " over a second pass of the K steps, right after "
+                                            "the timed region"},
             "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
                        "reasons": clocks.get("reasons", []), "samples": clocks.get("samples")},
             "e2e": {"value": round(elems_total * BYTES_PER_ELEM / (e2e_ms * 1e-3) / 1e9, 3),
@@ -687,7 +737,8 @@ def bench_ours(args):
                     "d2h_bytes_per_step": C.numel() + S.numel(), "ms_per_step": round(e2e_ms, 3),
                     "matches_device_path": same,
                     "pipeline": f"HostPipeline, 2 device buffer sets, {e2e_steps} steps timed"},
-            "gpu_launches": 2 * args.steps,   # in the timed region (amax + cast per step)
+            # in the timed region: the fused kernel, or amax + cast, per step
+            "gpu_launches": (1 if fused else 2) * args.steps,
             "parity": parity,
             "sustained": {"steps": sus_steps, "ms_per_step": round(sus_ms / sus_steps, 5),
                           "value": round(elems_total * BYTES_PER_ELEM /
@@ -715,6 +766,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["auto", "two", "fused"], default="auto",
+                    help="fused: one kernel per step; two: amax kernel + cast kernel; "
+                         "auto: fused for per-rank problems of >= 14336 x 32768 elements")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="how ranks combine the amax when --gpus > 1")
     args = ap.parse_args()
