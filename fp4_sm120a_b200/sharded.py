@@ -6,12 +6,17 @@ column-major view each rank holds an m x n_r matrix (m = cols, n_r = its rows),
 i.e. columns [n_offset, n_offset + n_r) of the full m x n_total problem.  One
 step is
     local amax (nvfp4_amax_bf16)
-    -> max-allreduce of that scalar (NCCL over NVLink; the only exchange)
+    -> combination of that scalar across the ranks, the only exchange:
+       exchange="nccl", an NCCL int32-MAX all-reduce over NVLink between the
+       two kernels; exchange="peer", inside the cast kernel, which publishes
+       and reads the ranks' amax over NVLink peer memory
     -> RHT GEMM + NVFP4 cast of the shard with the full problem's RNG
-       coordinates (nvfp4_rht_gemm_ntt_w_sfc_sharded),
+       coordinates (nvfp4_rht_gemm_ntt_w_sfc_sharded[_exchange]),
 so the per-rank outputs concatenated along the column dimension equal the
-single-GPU result bit for bit.  The reference has no multi-GPU path; this
-follows the row-sharding its north-star configuration asks for.
+single-GPU result bit for bit.  With fused=True one kernel computes the
+shard's amax, exchanges it over peer memory and casts.  The reference has no
+multi-GPU path; this follows the row-sharding its north-star configuration
+asks for.
 """
 from __future__ import annotations
 
