@@ -556,6 +556,10 @@ def bench_ours(args):
     C = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
     S = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
     amax = torch.empty(1, dtype=torch.float32, device="cuda")
+    # the two-kernel step's amax words, alternating between steps (the chained
+    # amax kernel clears the other one for the next step: no memset)
+    words = torch.zeros(2, dtype=torch.float32, device="cuda")
+    nstep = [0]
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
@@ -568,17 +572,22 @@ def bench_ours(args):
                 ev[1].record(stream)
             return
         # amax pre-pass -> exchange of the scalar -> RHT + NVFP4 cast.  With the
-        # peer exchange the cast kernel itself combines the ranks' amax.
-        nv.amax_bf16(A, m * n, amax, stream)
+        # peer exchange the cast kernel itself combines the ranks' amax.  The
+        # amax kernel runs chained: it starts while the previous step's cast
+        # drains (A is not written by it) and needs no memset.
+        i = nstep[0]
+        nstep[0] += 1
+        am = words[i % 2:i % 2 + 1]
+        nv.amax_bf16_chained(A, m * n, am, words[(i + 1) % 2:(i + 1) % 2 + 1], stream)
         if qz.peer is None:
-            combine_amax(amax)
+            combine_amax(am)
         if ev is not None:
             ev[0].record(stream)
         if qz.peer is None:
-            nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, amax, rng_state, qz.n_offset,
+            nv.rht_gemm_ntt_w_sfc_sharded(m, n, A, B, C, S, am, rng_state, qz.n_offset,
                                           n_total, 0, stream, 2048, stochastic_rounding=True)
         else:
-            nv.rht_gemm_ntt_w_sfc_sharded_exchange(m, n, A, B, C, S, amax, amax, rng_state,
+            nv.rht_gemm_ntt_w_sfc_sharded_exchange(m, n, A, B, C, S, am, am, rng_state,
                                                    qz.n_offset, n_total, qz.peer, 0, stream,
                                                    2048, stochastic_rounding=True)
         if ev is not None:
@@ -650,6 +659,8 @@ def bench_ours(args):
     if ws > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms_total, rht_ms, sus_ms = tt.tolist()
+    if not fused:
+        amax = words[(nstep[0] - 1) % 2:(nstep[0] - 1) % 2 + 1]   # the last step's amax
     parity = check_parity(torch, dist, nv, qz, A, B, C, S, amax, rng_state, ws, rank, fused)
     ms_step = ms_total / args.steps
     elems_total = m * n_total

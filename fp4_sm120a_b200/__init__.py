@@ -5,6 +5,7 @@ scaled FP8 conversions of Harry-Chen/fp4_sm120a, behind a C ABI
 from ._native import NVFP4Error, library_path, load  # noqa: F401
 from .ops import (  # noqa: F401
     amax_bf16,
+    amax_bf16_chained,
     cvt_fp32_to_fp4_4x_sr,
     device_error,
     hadamard16,

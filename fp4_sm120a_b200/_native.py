@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_quantize_rowwise_bf16_sr": ([c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p], c_int),
     "nvfp4_amax_bf16": ([c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "nvfp4_amax_bf16_chained": ([c_void_p, c_size_t, c_void_p, c_void_p, c_void_p], c_int),
     "nvfp4_mul_cvt_fp8_2x": ([c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_size_t,
                               c_void_p], c_int),
     "nvfp4_mul_cvt_fp8_4x": ([c_void_p, c_int, c_void_p, c_int, c_size_t, c_void_p, c_int,

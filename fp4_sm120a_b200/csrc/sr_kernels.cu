@@ -238,10 +238,18 @@ __global__ void __launch_bounds__(256) k_quantize_rowwise_8x_sr(
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) k_amax_bf16(const uint4* __restrict__ x, size_t nvec,
                                                    const uint16_t* __restrict__ tail, int ntail,
-                                                   uint32_t* __restrict__ out_bits) {
+                                                   uint32_t* __restrict__ out_bits,
+                                                   uint32_t* __restrict__ clear_bits) {
   // The next kernel (the cast) may launch now; it waits for this one to
   // complete before it reads the amax.
   asm volatile("griddepcontrol.launch_dependents;");
+  if (clear_bits != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+    // Chained form: this launch may overlap the previous kernel of the stream,
+    // which can still be reading *clear_bits; only this thread waits for it
+    // to complete before clearing the word for the next launch.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    *clear_bits = 0u;
+  }
   uint32_t m2 = 0;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
@@ -351,7 +359,39 @@ NVFP4_API int nvfp4_amax_bf16(const void* x, size_t n, float* out, nvfp4_stream_
   if (blocks == 0) blocks = 1;
   k_amax_bf16<<<(unsigned)blocks, 512, 0, st>>>(
       reinterpret_cast<const uint4*>(x), nvec,
-      reinterpret_cast<const uint16_t*>(x) + nvec * 8, ntail, reinterpret_cast<uint32_t*>(out));
+      reinterpret_cast<const uint16_t*>(x) + nvec * 8, ntail, reinterpret_cast<uint32_t*>(out),
+      nullptr);
+  return cuda_status(cudaGetLastError());
+}
+
+NVFP4_API int nvfp4_amax_bf16_chained(const void* x, size_t n, float* out, float* clear,
+                                      nvfp4_stream_t stream) {
+  if (!out || !clear || out == clear) return NVFP4_ERR_INVALID_ARGUMENT;
+  if (n > 0 && !x) return NVFP4_ERR_INVALID_ARGUMENT;
+  if ((uintptr_t)x % 16) return NVFP4_ERR_MISALIGNED;
+  int sms = 0;
+  if (int e = device_sm_count(&sms)) return e;
+  const size_t nvec = n / 8;
+  const int ntail = (int)(n % 8);
+  size_t blocks = (nvec + 511) / 512;
+  if (blocks > (size_t)sms * 4) blocks = (size_t)sms * 4;
+  if (blocks == 0) blocks = 1;
+  // A programmatic dependent of the previous kernel of the stream: its blocks
+  // start while that kernel drains.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(512);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaError_t e = cudaLaunchKernelEx(
+          &cfg, k_amax_bf16, reinterpret_cast<const uint4*>(x), nvec,
+          reinterpret_cast<const uint16_t*>(x) + nvec * 8, ntail,
+          reinterpret_cast<uint32_t*>(out), reinterpret_cast<uint32_t*>(clear)))
+    return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
 

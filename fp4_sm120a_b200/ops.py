@@ -180,6 +180,13 @@ def amax_bf16(x: Ptr, n: int, out: Ptr, stream=None) -> None:
     call("nvfp4_amax_bf16", _ptr(x), n, _ptr(out), _stream(stream))
 
 
+def amax_bf16_chained(x: Ptr, n: int, out: Ptr, clear: Ptr, stream=None) -> None:
+    """amax into *out (which must hold +0) and clear *clear for the next step,
+    without a memset, overlapping the previous kernel's tail (see
+    nvfp4_amax_bf16_chained)."""
+    call("nvfp4_amax_bf16_chained", _ptr(x), n, _ptr(out), _ptr(clear), _stream(stream))
+
+
 DTYPE_CODES = {"f32": 0, "bf16": 1, "f16": 2}
 FP8_FORMATS = {"e4m3": 0, "e5m2": 1}
 

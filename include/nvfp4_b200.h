@@ -226,6 +226,18 @@ NVFP4_API int nvfp4_quantize_rowwise_bf16_sr(int rows, int cols, const void* X,
  * produces it. */
 NVFP4_API int nvfp4_amax_bf16(const void* x, size_t n, float* out, nvfp4_stream_t stream);
 
+/* The same amax for a stream of steps, without the memset: *out must already
+ * hold +0 (a zeroed word, or the `clear` of the previous chained call), and the
+ * call sets *clear to +0 for the next one, so two words alternate between
+ * consecutive steps (step i: out = w[i % 2], clear = w[(i + 1) % 2]; both
+ * zeroed once before the first step).  The kernel is launched as a
+ * programmatic dependent of the previous kernel of the stream: it reads x
+ * while that kernel drains, and only the clearing of *clear waits for it to
+ * complete.  So x must not be written by the previous kernel of the stream.
+ * No reference counterpart (see nvfp4_amax_bf16). */
+NVFP4_API int nvfp4_amax_bf16_chained(const void* x, size_t n, float* out, float* clear,
+                                      nvfp4_stream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Scaled FP8 conversions (include/nvfp4_fp8.cuh) over batches of groups    */
 /* ---------------------------------------------------------------------- */

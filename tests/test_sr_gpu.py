@@ -220,3 +220,35 @@ def test_amax_large_tensors_vs_torch(nvlib, n):
         assert torch.isnan(out).all(), pos
         xb[pos] = saved
     assert nvlib.device_error() == 0
+
+
+def test_amax_chained_over_steps(nvlib):
+    """nvfp4_amax_bf16_chained over several back-to-back steps, each followed
+    by a cast: every step's amax equals torch's max of |x| of its input, the
+    word it clears reads +0 afterwards, and the casts equal those of the
+    memset + amax path."""
+    m, n = 1024, 4096
+    B = nvlib.hadamard16(device="cuda")
+    rs = torch.tensor([5, 0], dtype=torch.int64, device="cuda")
+    words = torch.zeros(2, dtype=torch.float32, device="cuda")
+    am_ref = torch.empty(1, dtype=torch.float32, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    xs = [(torch.randn(m * n, device="cuda", generator=g) * (i + 1)).to(torch.bfloat16)
+          for i in range(5)]
+    C = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
+    S = torch.empty((m, n // 16), dtype=torch.uint8, device="cuda")
+    C2, S2 = torch.empty_like(C), torch.empty_like(S)
+    for i, x in enumerate(xs):
+        out, clear = words[i % 2:i % 2 + 1], words[(i + 1) % 2:(i + 1) % 2 + 1]
+        nvlib.amax_bf16_chained(x, m * n, out, clear)
+        nvlib.rht_gemm_ntt_w_sfc(m, n, x, B, C, S, out, rs, 0, None, 2048,
+                                 stochastic_rounding=True)
+        nvlib.amax_bf16(x, m * n, am_ref)
+        nvlib.rht_gemm_ntt_w_sfc(m, n, x, B, C2, S2, am_ref, rs, 0, None, 2048,
+                                 stochastic_rounding=True)
+        torch.cuda.synchronize()
+        want = x.float().abs().max().view(1)
+        assert torch.equal(out.view(torch.int32), want.view(torch.int32)), i
+        assert float(clear.item()) == 0.0 and int(clear.view(torch.int32).item()) == 0
+        assert torch.equal(C, C2) and torch.equal(S, S2)
+    assert nvlib.device_error() == 0
