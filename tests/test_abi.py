@@ -138,3 +138,16 @@ def test_noalloc_rejects_more_units_than_its_scratch_counts(nvlib):
                                               2048, 1, 0)
     assert rc == 7, lib.nvfp4_status_string(rc)
     assert b"scratch" in lib.nvfp4_status_string(7)
+
+
+def test_amax_chained_validates_arguments(nvlib):
+    """The chained amax needs two distinct words (the one it accumulates into
+    and the one it clears for the next step) and refuses anything else before
+    any CUDA call."""
+    from fp4_sm120a_b200 import _native
+    lib = _native.load()
+    assert lib.nvfp4_amax_bf16_chained(16, 8, 64, 64, None) == 2     # out == clear
+    assert lib.nvfp4_amax_bf16_chained(16, 8, None, 64, None) == 2
+    assert lib.nvfp4_amax_bf16_chained(16, 8, 64, None, None) == 2
+    assert lib.nvfp4_amax_bf16_chained(None, 8, 64, 128, None) == 2   # no input
+    assert lib.nvfp4_amax_bf16_chained(18, 8, 64, 128, None) == 3     # misaligned input
